@@ -1,0 +1,333 @@
+"""SwiGLU-MLP fwd+bwd benchmark on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: config 2 of the benchmark, one SwiGLU MLP block in bf16,
+M=11136 D=3584 H=14336 Dout=3584, forward + recompute backward through the
+public API (SwiGLUMLPCustom / SwiGLUMemoryOptimizedFunction), seeded synthetic
+inputs (x, grad_y ~ N(0,1); W ~ N(0, fan_in^-1/2)). FLOPs per step
+6*M*(2H*D + H*Dout) = 10.2991 TFLOP (recompute and pointwise work not counted).
+
+  value      device-timed whole-job TFLOP/s, inputs resident in HBM (every
+             step's working set, >= 1.5 GB, exceeds the 126 MB L2)
+  e2e        same metric through the public API with host buffers: pinned
+             x and grad_y copied in and grad_x copied out every step
+  roofline   the dominant kernel's algorithmic TFLOP/s vs measured bf16 peak
+  cpu_baseline  the reference's pure-PyTorch fp32 path (CPU restatement),
+             timed on this host on a bounded row sample of the same shapes
+
+For N > 1 the block is tensor-parallel (tp.py): W1 column-sharded with
+left/gate pairs together, W2 row-sharded, x/grad_y all-gathered and the
+partial y / grad_x reduce-scattered over NCCL; the total workload stays
+config 2 (strong scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "swiglu-recompute_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+CFG = dict(M=11136, D=3584, H=14336, Dout=3584)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "SwiGLU-MLP fwd+bwd TFLOP/s (bf16, M=11136 D=3584 H=14336 Dout=3584)"
+
+
+def flops_fwd_bwd(M, D, H, Dout):
+    return 6.0 * M * (2 * H * D + H * Dout)
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "traffic.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU arm
+def cpu_reference_sample(seconds=12.0, rows=256):
+    """The reference's fp32 path (oracle restatement) on this host's cores, on a
+    `rows`-row slice of the config-2 shapes. Returns (TFLOP/s, cores, sample)."""
+    from oracle import swiglu_oracle as O
+
+    D, H, Dout = CFG["D"], CFG["H"], CFG["Dout"]
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, w1, w2, gy = O.make_inputs(rows, D, H, Dout, seed=0, dtype=torch.float32)
+    O.mlp_forward_backward(x[:16], w1, w2, gy[:16])            # warm-up
+    fl = flops_fwd_bwd(rows, D, H, Dout)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        O.mlp_forward_backward(x, w1, w2, gy)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    return fl / best / 1e12, torch.get_num_threads(), (
+        f"fp32 fwd+bwd of {rows} of {CFG['M']} rows at D={D} H={H} Dout={Dout}, "
+        f"best of {len(times)} (wall clock)")
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    tf, cores, sample = cpu_reference_sample(seconds=max(6.0, 2.0 * (args.steps + args.warmup)))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tf, 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 single SwiGLU block fwd+bwd (row sample)", **CFG},
+        "cpu_baseline": {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tf, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU arm
+def _inputs(dev, dtype=torch.bfloat16):
+    from oracle.swiglu_oracle import make_inputs
+    x, w1, w2, gy = make_inputs(CFG["M"], CFG["D"], CFG["H"], CFG["Dout"], seed=0, dtype=dtype)
+    return x, w1, w2, gy
+
+
+def kernel_breakdown(x, w1, w2, gy, iters):
+    """Per-kernel device time of one fwd+bwd, events between launches on the
+    launching stream. Returns {name: ms per launch}."""
+    from swiglu_b200 import ops
+    from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+
+    st = torch.cuda.current_stream()
+    names = ["gemm1_swiglu", "gemm2_y", "dw2_hprologue", "gradh_dswiglu_inplace", "dw1", "dx"]
+    acc = {n: 0.0 for n in names}
+    for _ in range(iters):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        ev[0].record(st)
+        preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+        ev[1].record(st)
+        ops.matmul(h, w2, a_t=False, b_t=True)
+        ev[2].record(st)
+        del h
+        ops.bwd_dw2(gy, preact, layout=LAYOUT_STD)
+        ev[3].record(st)
+        ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD)
+        ev[4].record(st)
+        ops.matmul(preact, x, a_t=True, b_t=False)
+        ev[5].record(st)
+        ops.matmul(preact, w1, a_t=False, b_t=False)
+        ev[6].record(st)
+        torch.cuda.synchronize()
+        for i, n in enumerate(names):
+            acc[n] += ev[i].elapsed_time(ev[i + 1])
+    return {n: v / iters for n, v in acc.items()}
+
+
+def kernel_flops(M, D, H, Dout):
+    g1 = 2.0 * M * D * 2 * H
+    g2 = 2.0 * M * H * Dout
+    return {"gemm1_swiglu": g1, "gemm2_y": g2, "dw2_hprologue": g2, "gradh_dswiglu_inplace": g2,
+            "dw1": g1, "dx": g1}
+
+
+def run_ours_single(args):
+    import swiglu_recompute as SR
+    from swiglu_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, D, H, Dout = CFG["M"], CFG["D"], CFG["H"], CFG["Dout"]
+    x, w1, w2, gy = _inputs(dev)
+    model = SR.SwiGLUMLPCustom(D, H, Dout, dtype=torch.bfloat16).to(dev)
+    with torch.no_grad():
+        model.w1.copy_(w1)
+        model.w2.copy_(w2)
+    params = list(model.parameters())
+    xd, gyd = x.to(dev), gy.to(dev)
+
+    def step():
+        xi = xd.detach().requires_grad_(True)
+        y = model(xi)
+        return torch.autograd.grad(y, [xi] + params, gyd)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert ops.device_status(0) == 0, "kernel pipeline timeout during warm-up"
+
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        time.sleep(0.3)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    fl = flops_fwd_bwd(M, D, H, Dout)
+    value = fl / (ms * 1e-3) / 1e12
+
+    # End to end through the public API with host buffers.
+    x_h = x.pin_memory()
+    gy_h = gy.pin_memory()
+    dx_h = torch.empty((M, D), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xi = x_h.to(dev, non_blocking=True).requires_grad_(True)
+        gyi = gy_h.to(dev, non_blocking=True)
+        y = model(xi)
+        gx, gw1, gw2 = torch.autograd.grad(y, [xi] + params, gyi)
+        dx_h.copy_(gx, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    e3.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3) / args.steps
+    h2d = x_h.numel() * 2 + gy_h.numel() * 2
+    d2h = dx_h.numel() * 2
+
+    # Per-kernel device times on the launching stream; dominant kernel roofline.
+    w1d, w2d = model.w1.detach(), model.w2.detach()
+    kt = kernel_breakdown(xd, w1d, w2d, gyd, iters=max(3, min(args.steps, 10)))
+    kf = kernel_flops(M, D, H, Dout)
+    dom = max(kt, key=kt.get)
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    ach = kf[dom] / (kt[dom] * 1e-3) / 1e12
+    assert ops.device_status(0) == 0, "kernel pipeline timeout"
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "cfg2: one SwiGLU MLP block fwd+bwd, recompute Function", **CFG,
+                   "parallelism": "tp1", "l2": "working set > L2 (preact alone 609 MiB)"},
+        "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 6 * args.steps,
+        "frac_of_peak": {"sustained": round(value / peak, 4),
+                         "burst": round(value / float(peaks["bf16_tflops"]), 4), "source": peak_src},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": profile_traffic(),
+                     "peak_kind": f"bf16_tflops_sustained ({peak_src})"},
+        "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        tf, cores, sample = cpu_reference_sample(seconds=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                "sample": sample}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    if args.gpus == 1 and world == 1:
+        line = run_ours_single(args)
+        print(json.dumps(line), flush=True)
+        return
+    from swiglu_b200 import tp
+    line = tp.bench_tp(args, CFG, flops_fwd_bwd, METRIC, ClockSampler, load_peaks, cpu_reference_sample)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

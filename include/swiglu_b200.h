@@ -1,0 +1,145 @@
+/*
+ * swiglu_b200.h - C ABI of the B200 (sm_100a) SwiGLU-MLP recompute hot path.
+ *
+ * Plain pointers, sizes and enums only: no framework types cross this
+ * boundary. Every tensor is dense, row-major and contiguous; every pointer is
+ * device memory on the CURRENT CUDA device; `stream` is a cudaStream_t (NULL =
+ * legacy default stream). All work is enqueued asynchronously on `stream`;
+ * no entry point allocates device memory (outputs and workspaces are owned
+ * and passed in by the caller).
+ *
+ * Shapes follow the reference (swiglu_recompute.py:12-13):
+ *   x [M, D]   W1 [2H, D]  (or Wt = W1^T [D, 2H], standard or packed)
+ *   W2 [Dout, H]   preact [M, 2H]   h [M, H]   y [M, Dout]
+ *
+ * Reference citations are file:line inside tongzhou8086/swiglu-recompute.
+ * The reference is Python; each entry point below is the native replacement
+ * of the Python function cited beside it.
+ */
+#ifndef SWIGLU_B200_H
+#define SWIGLU_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SWIGLU_B200_ABI_VERSION 1
+
+/* Status codes returned by every entry point. */
+enum swiglu_status {
+  SWIGLU_OK = 0,
+  SWIGLU_ERR_INVALID_ARGUMENT = 1,   /* a shape/dtype/layout precondition failed (the reference's AssertionError) */
+  SWIGLU_ERR_MISALIGNED = 2,         /* pointer or row pitch not 16-byte aligned (TMA requirement) */
+  SWIGLU_ERR_UNSUPPORTED_DEVICE = 3, /* current device is not compute capability 10.x (B200) */
+  SWIGLU_ERR_CUDA = 4,               /* a CUDA runtime or driver call failed */
+  SWIGLU_ERR_DEVICE_TIMEOUT = 5      /* a kernel's bounded pipeline wait expired (see swiglu_b200_device_status) */
+};
+
+/* Element types. */
+enum swiglu_dtype { SWIGLU_F32 = 0, SWIGLU_BF16 = 1 };
+
+/* Column layout of preact / the first-layer weight over its 2H axis.
+ * STD: [left | gate] (swiglu_recompute.py:29).
+ * PACKED128: [left0|gate0|left1|gate1|...] in 128-column chunks
+ *            (fused_forward_packed.py:77-92, BLOCK_SIZE_N_HALF = 128). */
+enum swiglu_layout { SWIGLU_LAYOUT_STD = 0, SWIGLU_LAYOUT_PACKED128 = 1 };
+
+/* Storage form of the first-layer weight.
+ * ROWS: W1 [2H, D], the nn.Linear layout of SwiGLUMLPCustom (swiglu_recompute.py:92).
+ * T:    W1^T [D, 2H]: `w1t` of SwiGLUMLPFused (fused_forward.py:299) or
+ *       `packed_weight` of SwiGLUMLPPackedFused (fused_forward_packed.py:331). */
+enum swiglu_w1_form { SWIGLU_W1_ROWS = 0, SWIGLU_W1_T = 1 };
+
+/* ABI version of the loaded library (== SWIGLU_B200_ABI_VERSION). */
+int swiglu_b200_abi_version(void);
+
+/* Human-readable name of a status code. */
+const char* swiglu_b200_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+const char* swiglu_b200_last_error_message(void);
+
+/* Reads (and optionally clears) the device status word of the current device:
+ * a bit mask of kernel pipeline timeouts. Synchronises the device. 0 = healthy. */
+int swiglu_b200_device_status(uint32_t* bits, int clear);
+
+/* One launch: preact [M, 2H] = x [M, K] . W1^T and h [M, H] = left * silu(gate).
+ * h may be NULL (preact only).
+ *   w_form = T, layout = STD:       fused_matmul_swiglu_save_preact   fused_forward.py:188-256
+ *   w_form = T, layout = PACKED128: fused_swiglu_save_preact_packed    fused_forward_packed.py:186-216
+ *                                   (and fused_forward_packed_canon.py:103-134)
+ *   w_form = ROWS, layout = STD:    `x @ W1.t()` + `_swiglu_forward_logic` swiglu_recompute.py:61,64
+ * h_from_rounded_preact = 1 computes h from the stored (rounded) preact, as the
+ * recompute Function does (swiglu_recompute.py:64); 0 computes it from the f32
+ * accumulator, as the fused Triton kernels do (fused_forward.py:177).
+ * group_size_m: L2 swizzle group of the tile order (fused_forward.py:192). */
+int swiglu_b200_fused_matmul_swiglu_save_preact(const void* x, const void* w, void* preact, void* h, int64_t M,
+                                                int64_t K, int64_t H, int dtype, int w_form, int layout,
+                                                int h_from_rounded_preact, int group_size_m, void* stream);
+
+/* C [M, N] = op(A) . op(B), f32 accumulation; out_dtype may be F32 for a bf16 GEMM.
+ *   a_layout 0: A stored [M, K];  1: A stored [K, M] (op(A) = stored^T)
+ *   b_layout 0: B stored [K, N];  1: B stored [N, K] (op(B) = stored^T)
+ * Replaces the torch.matmul calls of the path: y = h @ W2.t() (swiglu_recompute.py:65),
+ * grad_W1 = grad_preact.t() @ x (:76), grad_x = grad_preact @ W1 (:77), and their
+ * w1t/packed forms (fused_forward.py:272,282-283; fused_forward_packed.py:301,314-315). */
+int swiglu_b200_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout,
+                       int b_layout, int dtype, int out_dtype, int group_size_m, void* stream);
+
+/* dW2 [Dout, H] = grad_y^T . h with h = left * silu(gate) recomputed from preact
+ * inside the GEMM's operand prologue (no [M, H] buffer).
+ * Replaces `h = _swiglu_forward_logic(preact); grad_W2 = grad_y.t() @ h`
+ * (swiglu_recompute.py:71-73; packed: fused_forward_packed.py:310-311). */
+int swiglu_b200_bwd_dw2(const void* grad_y, const void* preact, void* dw2, int64_t M, int64_t H, int64_t Dout,
+                        int dtype, int layout, void* stream);
+
+/* grad_h = grad_y [M, Dout] . W2 [Dout, H], never stored: the GEMM epilogue turns
+ * each tile into grad_left / grad_gate and overwrites preact with grad_preact.
+ * Replaces `grad_h = grad_y @ W2; grad_preact = _swiglu_backward_logic(preact, grad_h)`
+ * (swiglu_recompute.py:74-75; packed: fused_forward_packed.py:312-313). */
+int swiglu_b200_bwd_grad_preact_inplace(const void* grad_y, const void* w2, void* preact, int64_t M, int64_t H,
+                                        int64_t Dout, int dtype, int layout, void* stream);
+
+/* h [M, H] = left * silu(gate) from preact [M, 2H].
+ * _swiglu_forward_logic (swiglu_recompute.py:26-30); packed: _h_from_packed_preact
+ * (fused_forward_packed.py:281-286). H % 8 == 0. */
+int swiglu_b200_forward_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout,
+                              void* stream);
+
+/* grad_preact [M, 2H] from preact [M, 2H] and grad_h [M, H] (grad_preact may alias preact).
+ * _swiglu_backward_logic (swiglu_recompute.py:33-49); packed: swiglu_packed_grad_de_from_preact
+ * (fused_forward_packed.py:262-277). H % 8 == 0. */
+int swiglu_b200_backward_logic(const void* preact, const void* grad_h, void* grad_preact, int64_t M, int64_t H,
+                               int dtype, int layout, void* stream);
+
+/* Chunk-interleave a [K, 2*N_half] weight ([left | gate] -> packed), or undo it (unpack = 1).
+ * pack_swiglu_weight_chunked_torch / unpack_swiglu_weight_chunked_torch
+ * (fused_forward_packed.py:77-107). src and dst must not alias. */
+int swiglu_b200_pack_weight_chunked(const void* src, void* dst, int64_t K, int64_t N_half, int64_t block_n_half,
+                                    int dtype, int unpack, void* stream);
+
+/* Whole forward of one MLP block: preact (saved for backward), h (caller's
+ * transient workspace [M, H]) and y [M, Dout].
+ * SwiGLUMemoryOptimizedFunction.forward (swiglu_recompute.py:59-66),
+ * SwiGLUFusedForwardFunction.forward (fused_forward.py:265-273),
+ * SwiGLUPackedFusedFunction.forward (fused_forward_packed.py:294-302). */
+int swiglu_b200_mlp_forward(const void* x, const void* w1, const void* w2, void* preact, void* h_workspace,
+                            void* y, int64_t M, int64_t D, int64_t H, int64_t Dout, int dtype, int w_form,
+                            int layout, int h_from_rounded_preact, void* stream);
+
+/* Whole backward of one MLP block. preact is consumed: on return it holds
+ * grad_preact. dw1 has the form of w1 (ROWS: [2H, D]; T: [D, 2H] in `layout`).
+ * SwiGLUMemoryOptimizedFunction.backward (swiglu_recompute.py:68-78),
+ * SwiGLUFusedForwardFunction.backward (fused_forward.py:276-284),
+ * SwiGLUPackedFusedFunction.backward (fused_forward_packed.py:305-316). */
+int swiglu_b200_mlp_backward(const void* x, const void* w1, const void* w2, void* preact, const void* grad_y,
+                             void* dx, void* dw1, void* dw2, int64_t M, int64_t D, int64_t H, int64_t Dout,
+                             int dtype, int w_form, int layout, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWIGLU_B200_H */

@@ -1,0 +1,144 @@
+"""CPU oracle of the SwiGLU-MLP recompute path. TEST INFRASTRUCTURE ONLY.
+
+Only `tests/`, `__graft_entry__.smoke()` and `bench.py`'s CPU-baseline leg
+may import this module; it is the checker the native kernels are compared
+against, never part of the product path.
+
+A plain-PyTorch (CPU, fp32) restatement of tongzhou8086/swiglu-recompute's
+math, one function per reference function (file:line cited on each). The bf16
+mode reproduces the reference's rounding points: every GEMM output is rounded
+to bf16 once (cuBLAS, f32 accumulation), every compiled pointwise chain runs in
+f32 from bf16 inputs and rounds once on store (Inductor).
+
+Pinned against golden vectors produced by running the reference itself
+(tests/golden/make_golden.py -> tests/golden/*.npz, checked by
+tests/test_oracle_golden.py).
+"""
+from __future__ import annotations
+
+import torch
+
+STD, PACKED = "std", "packed"
+PACK_CHUNK = 128  # BLOCK_SIZE_N_HALF, fused_forward_packed.py:41
+
+
+def rel_max(a: torch.Tensor, b: torch.Tensor) -> float:
+    """max|a-b| / max|b| (bench_swiglu_recompute.py:39-41)."""
+    denom = b.float().abs().max().clamp_min(1e-6)
+    return ((a.float() - b.float()).abs().max() / denom).item()
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def _round(t: torch.Tensor, bf16: bool) -> torch.Tensor:
+    return _bf16(t) if bf16 else t
+
+
+def col_index(H: int, layout: str, block: int = PACK_CHUNK):
+    """Column index of left[j] and gate[j] in a [.., 2H] row.
+
+    std: [left | gate] (swiglu_recompute.py:29 `chunk(2)`);
+    packed: [left0|gate0|left1|...] in `block` chunks (fused_forward_packed.py:77-92).
+    """
+    j = torch.arange(H)
+    if layout == STD:
+        return j, j + H
+    assert H % block == 0
+    c, off = j // block, j % block
+    return c * 2 * block + off, c * 2 * block + block + off
+
+
+def pack_weight_chunked(weight: torch.Tensor, block: int = PACK_CHUNK) -> torch.Tensor:
+    """[K, 2N] standard -> chunk-interleaved (fused_forward_packed.py:77-92)."""
+    K, n2 = weight.shape
+    li, gi = col_index(n2 // 2, PACKED, block)
+    out = torch.empty_like(weight)
+    out[:, li] = weight[:, : n2 // 2]
+    out[:, gi] = weight[:, n2 // 2:]
+    return out
+
+
+def unpack_weight_chunked(packed: torch.Tensor, block: int = PACK_CHUNK) -> torch.Tensor:
+    """Inverse of pack_weight_chunked (fused_forward_packed.py:95-107)."""
+    K, n2 = packed.shape
+    li, gi = col_index(n2 // 2, PACKED, block)
+    return torch.cat([packed[:, li], packed[:, gi]], dim=1)
+
+
+def forward_logic(preact: torch.Tensor, layout: str = STD, bf16: bool = False) -> torch.Tensor:
+    """h = left * silu(gate) (swiglu_recompute.py:26-30; packed gather
+    fused_forward_packed.py:281-286). f32 math, one rounding."""
+    H = preact.shape[-1] // 2
+    li, gi = col_index(H, layout)
+    p = preact.float()
+    left, gate = p[:, li], p[:, gi]
+    return _round(left * (gate * torch.sigmoid(gate)), bf16)
+
+
+def backward_logic(preact: torch.Tensor, grad_h: torch.Tensor, layout: str = STD,
+                   bf16: bool = False) -> torch.Tensor:
+    """grad_preact via the explicit SiLU derivative (swiglu_recompute.py:33-49;
+    packed: fused_forward_packed.py:247-259)."""
+    H = preact.shape[-1] // 2
+    li, gi = col_index(H, layout)
+    p = preact.float()
+    left, gate = p[:, li], p[:, gi]
+    g = grad_h.float()
+    sig = torch.sigmoid(gate)
+    silu = gate * sig
+    dsilu = sig + silu * (1.0 - sig)
+    out = torch.empty_like(p)
+    out[:, li] = g * silu
+    out[:, gi] = g * left * dsilu
+    return _round(out, bf16)
+
+
+def mlp_forward_backward(x, w1_rows, w2, grad_y, *, bf16: bool = False,
+                         h_from_accumulator: bool = False, layout: str = STD):
+    """One recompute fwd+bwd (SwiGLUMemoryOptimizedFunction, swiglu_recompute.py:58-78).
+
+    w1_rows is W1 [2H, D] with its 2H rows in `layout` order. With
+    h_from_accumulator the forward h comes from the unrounded GEMM result, as
+    in the fused Triton kernels (fused_forward.py:177,
+    fused_forward_packed.py:174-177); the backward is identical in all variants.
+    Returns dict(y, dx, dw1, dw2, preact).
+    """
+    x, w1, w2, gy = (t.float() for t in (x, w1_rows, w2, grad_y))
+    acc = x @ w1.t()                                        # :61
+    preact = _round(acc, bf16)
+    src = acc if h_from_accumulator else preact
+    h = forward_logic(src, layout, bf16)                    # :64
+    y = _round(h @ w2.t(), bf16)                            # :65
+    h_bwd = forward_logic(preact, layout, bf16)             # :71 recompute
+    dw2 = _round(gy.t() @ h_bwd, bf16)                      # :73
+    grad_h = _round(gy @ w2, bf16)                          # :74
+    gp = backward_logic(preact, grad_h, layout, bf16)       # :75
+    dw1 = _round(gp.t() @ x, bf16)                          # :76
+    dx = _round(gp @ w1, bf16)                              # :77
+    return {"y": y, "dx": dx, "dw1": dw1, "dw2": dw2, "preact": preact, "h": h}
+
+
+def ground_truth(x, w1, w2, grad_y):
+    """Autograd through the standard MLP (SwiGLUMLPGroundTruth, swiglu_recompute.py:101-118)."""
+    x = x.detach().clone().requires_grad_(True)
+    w1 = w1.detach().clone().requires_grad_(True)
+    w2 = w2.detach().clone().requires_grad_(True)
+    preact = x @ w1.t()
+    left, gate = preact.chunk(2, dim=-1)
+    y = (left * torch.nn.functional.silu(gate)) @ w2.t()
+    dx, dw1, dw2 = torch.autograd.grad(y, [x, w1, w2], grad_y)
+    return {"y": y.detach(), "dx": dx, "dw1": dw1, "dw2": dw2}
+
+
+def make_inputs(M: int, D: int, H: int, Dout: int, seed: int = 0, dtype=torch.float32):
+    """Seeded inputs with the distributions of the benchmark configs: x, grad_y ~
+    N(0,1); W1, W2 ~ N(0, fan_in^-1/2) (fused_forward.py:359-360). Drawn in
+    f32 on the CPU in the order x, W1, W2, grad_y, then cast."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, D, generator=g)
+    w1 = torch.randn(2 * H, D, generator=g) * D ** -0.5
+    w2 = torch.randn(Dout, H, generator=g) * H ** -0.5
+    gy = torch.randn(M, Dout, generator=g)
+    return tuple(t.to(dtype) for t in (x, w1, w2, gy))

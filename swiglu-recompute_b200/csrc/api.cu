@@ -1,0 +1,618 @@
+// Host side of the C ABI declared in include/swiglu_b200.h: argument checks,
+// TMA tensor-map encoding, kernel selection and launch. No allocation: every
+// buffer is the caller's.
+#include "swiglu_b200.h"
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "simt_kernels.cuh"
+
+namespace swiglu {
+
+// Bit mask of pipeline timeouts, one word per device (see ptx.cuh).
+__device__ uint32_t g_status_word;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SWIGLU_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::atomic<bool> ready{false};
+  int sms = 0;
+  int major = 0;
+  uint32_t* status = nullptr;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetDeviceFn = CUresult (*)(CUdevice*);
+
+// The device an entry point works on is the device of the context bound to
+// the calling thread (the one torch or any other runtime made current), so
+// this library and its caller agree even though they link different CUDA
+// runtimes. A thread that has never made a CUDA call (e.g. the autograd
+// engine's device thread) has no context bound; driver calls such as
+// cuTensorMapEncodeTiled would then fail with CUDA_ERROR_INVALID_CONTEXT, so
+// the runtime's current device's primary context is bound first.
+int resolve_device(int* out) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetDeviceFn get_device = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetDevice", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_device = reinterpret_cast<CtxGetDeviceFn>(p);
+  });
+  int rdev = 0;
+  cudaError_t e = cudaGetDevice(&rdev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  CUcontext ctx = nullptr;
+  CUdevice cdev = 0;
+  if (get_current && get_device && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr &&
+      get_device(&cdev) == CUDA_SUCCESS) {
+    if (static_cast<int>(cdev) != rdev) {
+      if ((e = cudaSetDevice(static_cast<int>(cdev))) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    }
+    *out = static_cast<int>(cdev);
+    return SWIGLU_OK;
+  }
+  if ((e = cudaSetDevice(rdev)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  *out = rdev;
+  return SWIGLU_OK;
+}
+
+int current_device(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaSuccess;
+  if (int rc = resolve_device(&dev)) return rc;
+  if (dev < 0 || dev >= kMaxDevices) return fail(SWIGLU_ERR_UNSUPPORTED_DEVICE, "device ordinal %d out of range", dev);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!d.ready.load(std::memory_order_relaxed)) {
+      if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+      if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute(CC major)");
+      void* sym = nullptr;
+      if ((e = cudaGetSymbolAddress(&sym, g_status_word)) != cudaSuccess)
+        return cuda_fail(e, "cudaGetSymbolAddress(status word)");
+      d.status = static_cast<uint32_t*>(sym);
+      d.ready.store(true, std::memory_order_release);
+    }
+  }
+  if (d.major != 10)
+    return fail(SWIGLU_ERR_UNSUPPORTED_DEVICE, "device %d has compute capability %d.x; this library targets sm_100a",
+                dev, d.major);
+  *out = &d;
+  return SWIGLU_OK;
+}
+
+// ------------------------------------------------------------ tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) return fail(SWIGLU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorName(err));
+  *out = fn;
+  return SWIGLU_OK;
+}
+
+// 2-D bf16 map over a row-major [outer, inner] view with row pitch `ld`
+// elements; 128-byte swizzled boxes of {64, box_outer}.
+int make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer,
+             const char* what) {
+  EncodeTiledFn fn;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "%s: base address is not 16-byte aligned", what);
+  if ((ld * 2) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "%s: row pitch of %llu elements is not a multiple of 8", what,
+                (unsigned long long)ld);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {64, box_outer};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SWIGLU_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", what, (int)r);
+  return SWIGLU_OK;
+}
+
+// Operand maps. K-major operand stored [rows][K]; MN-major stored [K][cols].
+int map_kmajor(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows,
+               const char* what) {
+  return make_map(m, p, K, rows, ld, box_rows, what);
+}
+int map_mnmajor(CUtensorMap* m, const void* p, int64_t K, int64_t cols, int64_t ld, const char* what) {
+  return make_map(m, p, cols, K, ld, 64, what);
+}
+
+// ------------------------------------------------------------ launching
+constexpr uint32_t kMnLbo = 64 * 64 * 2;  // one {64, 64} bf16 box
+constexpr uint32_t kMnSbo = 8 * 128;      // eight 128-byte swizzle rows
+
+template <class Cfg>
+int launch_tc(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = tc_gemm_kernel<Cfg>;
+  if (!(attr_set.load() & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+    attr_set.fetch_or(1ull << dev);
+  }
+  p.mn_lbo = kMnLbo;
+  p.mn_sbo = kMnSbo;
+  p.status = d.status;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < d.sms ? tiles : d.sms;
+  kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
+  return SWIGLU_OK;
+}
+
+template <bool A_MN, bool B_MN, int EPI, bool TRANSFORM>
+int launch_simt(const SimtParams& p, int ntile_cols, cudaStream_t st) {
+  dim3 grid(ntile_cols, (p.M + 63) / 64);
+  if (grid.y > 65535) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "M=%d too large for the fp32 path", p.M);
+  simt_gemm_f32_kernel<A_MN, B_MN, EPI, TRANSFORM><<<grid, 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fp32 GEMM launch");
+  return SWIGLU_OK;
+}
+
+int pointwise_grid(long long work, const DeviceInfo& d) {
+  long long g = (work + 255) / 256;
+  const long long cap = static_cast<long long>(d.sms) * 16;
+  if (g > cap) g = cap;
+  return g < 1 ? 1 : static_cast<int>(g);
+}
+
+bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffffLL; }
+
+int check_dtype(int dtype) {
+  if (dtype != SWIGLU_F32 && dtype != SWIGLU_BF16) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  return SWIGLU_OK;
+}
+int check_layout(int layout, int64_t H) {
+  if (layout != SWIGLU_LAYOUT_STD && layout != SWIGLU_LAYOUT_PACKED128)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "unknown layout %d", layout);
+  if (layout == SWIGLU_LAYOUT_PACKED128 && H % kPackChunk)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "packed layout needs H %% 128 == 0 (H=%lld)", (long long)H);
+  return SWIGLU_OK;
+}
+int check_dims(const char* what, int64_t a, int64_t b, int64_t c) {
+  if (!fits_int(a) || !fits_int(b) || !fits_int(c))
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "%s: dimensions must be in [0, 2^31)", what);
+  return SWIGLU_OK;
+}
+int check_mult8(const char* what, int64_t v) {
+  if (v % 8) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "%s=%lld must be a multiple of 8", what, (long long)v);
+  return SWIGLU_OK;
+}
+
+// ---------------------------------------------------------------- ops
+int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M, int64_t K, int64_t H, int dtype,
+                  int w_form, int layout, int rounded, int group_m, cudaStream_t st) {
+  if (int rc = check_dims("fused_matmul_swiglu_save_preact", M, K, 2 * H)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (w_form != SWIGLU_W1_ROWS && w_form != SWIGLU_W1_T)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "unknown w_form %d", w_form);
+  if (w_form == SWIGLU_W1_ROWS && layout != SWIGLU_LAYOUT_STD)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "the packed layout applies to the [D, 2H] weight form only");
+  if (K <= 0 || H <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K and H must be positive");
+  if (group_m < 1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "group_size_m must be >= 1");
+  if (M == 0) return SWIGLU_OK;
+  if (!x || !w || !preact) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  if (dtype == SWIGLU_F32) {
+    SimtParams p{};
+    p.a = static_cast<const float*>(x);
+    p.b = static_cast<const float*>(w);
+    p.out0 = static_cast<float*>(preact);
+    p.out1 = static_cast<float*>(h);
+    p.lda = K;
+    p.ldb = w_form == SWIGLU_W1_ROWS ? K : 2 * H;
+    p.ld0 = 2 * H;
+    p.ld1 = H;
+    p.M = (int)M, p.N = (int)H, p.K = (int)K, p.H = (int)H, p.layout = layout;
+    const int nt = (int)((H + 31) / 32);
+    return w_form == SWIGLU_W1_ROWS ? launch_simt<false, false, kEpiSwiglu, false>(p, nt, st)
+                                    : launch_simt<false, true, kEpiSwiglu, false>(p, nt, st);
+  }
+  if (int rc = check_mult8("K", K)) return rc;
+  if (int rc = check_mult8("H", H)) return rc;
+  TcParams p{};
+  if (int rc = map_kmajor(&p.tmA, x, M, K, K, 128, "x")) return rc;
+  if (w_form == SWIGLU_W1_ROWS) {
+    if (int rc = map_kmajor(&p.tmB, w, 2 * H, K, K, 128, "W1")) return rc;
+  } else {
+    if (int rc = map_mnmajor(&p.tmB, w, K, 2 * H, 2 * H, "Wt")) return rc;
+  }
+  p.out0 = preact;
+  p.out1 = h;
+  p.ld0 = 2 * H;
+  p.ld1 = H;
+  p.M = (int)M, p.N = (int)H, p.K = (int)K, p.H = (int)H, p.layout = layout;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((H + 127) / 128);
+  p.group_m = group_m;
+  p.flags = rounded ? kFlagHFromRounded : 0;
+  if (reinterpret_cast<uintptr_t>(preact) % 16 || (h && reinterpret_cast<uintptr_t>(h) % 16))
+    return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
+  return w_form == SWIGLU_W1_ROWS ? launch_tc<TcCfg<256, false, false, kEpiSwiglu, false, false>>(p, *d, st)
+                                  : launch_tc<TcCfg<256, false, true, kEpiSwiglu, false, false>>(p, *d, st);
+}
+
+int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout, int b_layout,
+              int dtype, int out_dtype, int group_m, cudaStream_t st) {
+  if (int rc = check_dims("matmul", M, N, K)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_dtype(out_dtype)) return rc;
+  if ((a_layout | b_layout) & ~1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "layout flags must be 0 or 1");
+  if (dtype == SWIGLU_F32 && out_dtype != SWIGLU_F32)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "an f32 GEMM writes f32");
+  if (K <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K must be positive");
+  if (group_m < 1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "group_size_m must be >= 1");
+  if (M == 0 || N == 0) return SWIGLU_OK;
+  if (!a || !b || !c) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  const bool a_mn = a_layout == 1;       // stored [K][M]
+  const bool b_mn = b_layout == 0;       // stored [K][N]
+  if (dtype == SWIGLU_F32) {
+    SimtParams p{};
+    p.a = static_cast<const float*>(a);
+    p.b = static_cast<const float*>(b);
+    p.out0 = static_cast<float*>(c);
+    p.lda = a_mn ? M : K;
+    p.ldb = b_mn ? N : K;
+    p.ld0 = N;
+    p.M = (int)M, p.N = (int)N, p.K = (int)K;
+    const int nt = (int)((N + 63) / 64);
+    if (a_mn) return b_mn ? launch_simt<true, true, kEpiStore, false>(p, nt, st)
+                          : launch_simt<true, false, kEpiStore, false>(p, nt, st);
+    return b_mn ? launch_simt<false, true, kEpiStore, false>(p, nt, st)
+                : launch_simt<false, false, kEpiStore, false>(p, nt, st);
+  }
+  // TMA row pitches must be multiples of 16 bytes: the contiguous dimension of
+  // each operand (K for a K-major operand, M or N for an MN-major one) and N
+  // for the output rows.
+  if (!a_mn || !b_mn) { if (int rc = check_mult8("K", K)) return rc; }
+  if (a_mn) { if (int rc = check_mult8("M", M)) return rc; }
+  if (int rc = check_mult8("N", N)) return rc;
+  TcParams p{};
+  if (a_mn) {
+    if (int rc = map_mnmajor(&p.tmA, a, K, M, M, "A")) return rc;
+  } else {
+    if (int rc = map_kmajor(&p.tmA, a, M, K, K, 128, "A")) return rc;
+  }
+  if (b_mn) {
+    if (int rc = map_mnmajor(&p.tmB, b, K, N, N, "B")) return rc;
+  } else {
+    if (int rc = map_kmajor(&p.tmB, b, N, K, K, 128, "B")) return rc;
+  }
+  if (reinterpret_cast<uintptr_t>(c) % 16) return fail(SWIGLU_ERR_MISALIGNED, "C must be 16-byte aligned");
+  p.out0 = c;
+  p.ld0 = N;
+  p.M = (int)M, p.N = (int)N, p.K = (int)K, p.H = 0, p.layout = 0;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((N + 255) / 256);
+  p.group_m = group_m;
+  const bool f32 = out_dtype == SWIGLU_F32;
+#define SWIGLU_MM(AM, BM_, F) launch_tc<TcCfg<256, AM, BM_, kEpiStore, false, F>>(p, *d, st)
+  if (f32) {
+    if (a_mn) return b_mn ? SWIGLU_MM(true, true, true) : SWIGLU_MM(true, false, true);
+    return b_mn ? SWIGLU_MM(false, true, true) : SWIGLU_MM(false, false, true);
+  }
+  if (a_mn) return b_mn ? SWIGLU_MM(true, true, false) : SWIGLU_MM(true, false, false);
+  return b_mn ? SWIGLU_MM(false, true, false) : SWIGLU_MM(false, false, false);
+#undef SWIGLU_MM
+}
+
+int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, int64_t Dout, int dtype, int layout,
+           cudaStream_t st) {
+  if (int rc = check_dims("bwd_dw2", M, 2 * H, Dout)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (H <= 0 || Dout <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "H and Dout must be positive");
+  if (!dw2 || (M > 0 && (!gy || !preact))) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  if (M == 0) {
+    cudaError_t e = cudaMemsetAsync(dw2, 0, Dout * H * (dtype == SWIGLU_F32 ? 4 : 2), st);
+    return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "cudaMemsetAsync(dW2)");
+  }
+  if (dtype == SWIGLU_F32) {
+    SimtParams p{};
+    p.a = static_cast<const float*>(gy);
+    p.b = static_cast<const float*>(preact);
+    p.out0 = static_cast<float*>(dw2);
+    p.lda = Dout;
+    p.ldb = 2 * H;
+    p.ld0 = H;
+    p.M = (int)Dout, p.N = (int)H, p.K = (int)M, p.H = (int)H, p.layout = layout;
+    return launch_simt<true, true, kEpiStore, true>(p, (int)((H + 63) / 64), st);
+  }
+  if (int rc = check_mult8("H", H)) return rc;
+  if (int rc = check_mult8("Dout", Dout)) return rc;
+  TcParams p{};
+  if (int rc = map_mnmajor(&p.tmA, gy, M, Dout, Dout, "grad_y")) return rc;
+  if (int rc = map_mnmajor(&p.tmB, preact, M, 2 * H, 2 * H, "preact")) return rc;
+  if (reinterpret_cast<uintptr_t>(dw2) % 16) return fail(SWIGLU_ERR_MISALIGNED, "dW2 must be 16-byte aligned");
+  p.out0 = dw2;
+  p.ld0 = H;
+  p.M = (int)Dout, p.N = (int)H, p.K = (int)M, p.H = (int)H, p.layout = layout;
+  p.tiles_m = (int)((Dout + 127) / 128);
+  p.tiles_n = (int)((H + 127) / 128);
+  p.group_m = 8;
+  return launch_tc<TcCfg<128, true, true, kEpiStore, true, false>>(p, *d, st);
+}
+
+int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int64_t H, int64_t Dout, int dtype,
+                   int layout, cudaStream_t st) {
+  if (int rc = check_dims("bwd_grad_preact_inplace", M, 2 * H, Dout)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (H <= 0 || Dout <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "H and Dout must be positive");
+  if (M == 0) return SWIGLU_OK;
+  if (!gy || !w2 || !preact) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  if (dtype == SWIGLU_F32) {
+    SimtParams p{};
+    p.a = static_cast<const float*>(gy);
+    p.b = static_cast<const float*>(w2);
+    p.out0 = static_cast<float*>(preact);
+    p.lda = Dout;
+    p.ldb = H;
+    p.ld0 = 2 * H;
+    p.M = (int)M, p.N = (int)H, p.K = (int)Dout, p.H = (int)H, p.layout = layout;
+    return launch_simt<false, true, kEpiDswiglu, false>(p, (int)((H + 63) / 64), st);
+  }
+  if (int rc = check_mult8("H", H)) return rc;
+  if (int rc = check_mult8("Dout", Dout)) return rc;
+  TcParams p{};
+  if (int rc = map_kmajor(&p.tmA, gy, M, Dout, Dout, 128, "grad_y")) return rc;
+  if (int rc = map_mnmajor(&p.tmB, w2, Dout, H, H, "W2")) return rc;
+  if (reinterpret_cast<uintptr_t>(preact) % 16) return fail(SWIGLU_ERR_MISALIGNED, "preact must be 16-byte aligned");
+  p.out0 = preact;
+  p.ld0 = 2 * H;
+  p.M = (int)M, p.N = (int)H, p.K = (int)Dout, p.H = (int)H, p.layout = layout;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((H + 255) / 256);
+  p.group_m = 16;
+  return launch_tc<TcCfg<256, false, true, kEpiDswiglu, false, false>>(p, *d, st);
+}
+
+int op_fwd_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout, cudaStream_t st) {
+  if (int rc = check_dims("forward_logic", M, 2 * H, 0)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (int rc = check_mult8("H", H)) return rc;
+  if (M == 0 || H == 0) return SWIGLU_OK;
+  if (!preact || !h) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(preact) % 16 || reinterpret_cast<uintptr_t>(h) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  const int grid = pointwise_grid(M * (H / 8), *d);
+  if (dtype == SWIGLU_F32)
+    swiglu_fwd_pointwise_kernel<float><<<grid, 256, 0, st>>>((const float*)preact, (float*)h, M, (int)H, layout);
+  else
+    swiglu_fwd_pointwise_kernel<__nv_bfloat16>
+        <<<grid, 256, 0, st>>>((const __nv_bfloat16*)preact, (__nv_bfloat16*)h, M, (int)H, layout);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "forward_logic launch");
+}
+
+int op_bwd_logic(const void* preact, const void* gh, void* gp, int64_t M, int64_t H, int dtype, int layout,
+                 cudaStream_t st) {
+  if (int rc = check_dims("backward_logic", M, 2 * H, 0)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (int rc = check_mult8("H", H)) return rc;
+  if (M == 0 || H == 0) return SWIGLU_OK;
+  if (!preact || !gh || !gp) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(preact) % 16 || reinterpret_cast<uintptr_t>(gh) % 16 ||
+      reinterpret_cast<uintptr_t>(gp) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "buffers must be 16-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  const int grid = pointwise_grid(M * (H / 8), *d);
+  if (dtype == SWIGLU_F32)
+    swiglu_bwd_pointwise_kernel<float>
+        <<<grid, 256, 0, st>>>((const float*)preact, (const float*)gh, (float*)gp, M, (int)H, layout);
+  else
+    swiglu_bwd_pointwise_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        (const __nv_bfloat16*)preact, (const __nv_bfloat16*)gh, (__nv_bfloat16*)gp, M, (int)H, layout);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "backward_logic launch");
+}
+
+int op_pack(const void* src, void* dst, int64_t K, int64_t Nh, int64_t B, int dtype, int unpack, cudaStream_t st) {
+  if (int rc = check_dtype(dtype)) return rc;
+  if (K < 0 || Nh < 0 || B <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "bad pack dimensions");
+  if (Nh % B) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "N_half=%lld must be a multiple of block_n_half=%lld",
+                          (long long)Nh, (long long)B);
+  if (K == 0 || Nh == 0) return SWIGLU_OK;
+  if (!src || !dst) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (src == dst) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "pack source and destination must not alias");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  const int grid = pointwise_grid(K * 2 * Nh, *d);
+  if (dtype == SWIGLU_F32)
+    pack_chunked_kernel<float><<<grid, 256, 0, st>>>((const float*)src, (float*)dst, K, Nh, B, unpack);
+  else
+    pack_chunked_kernel<__nv_bfloat16>
+        <<<grid, 256, 0, st>>>((const __nv_bfloat16*)src, (__nv_bfloat16*)dst, K, Nh, B, unpack);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "pack launch");
+}
+
+}  // namespace
+}  // namespace swiglu
+
+using namespace swiglu;
+
+extern "C" {
+
+int swiglu_b200_abi_version(void) { return SWIGLU_B200_ABI_VERSION; }
+
+const char* swiglu_b200_status_string(int status) {
+  switch (status) {
+    case SWIGLU_OK: return "SWIGLU_OK";
+    case SWIGLU_ERR_INVALID_ARGUMENT: return "SWIGLU_ERR_INVALID_ARGUMENT";
+    case SWIGLU_ERR_MISALIGNED: return "SWIGLU_ERR_MISALIGNED";
+    case SWIGLU_ERR_UNSUPPORTED_DEVICE: return "SWIGLU_ERR_UNSUPPORTED_DEVICE";
+    case SWIGLU_ERR_CUDA: return "SWIGLU_ERR_CUDA";
+    case SWIGLU_ERR_DEVICE_TIMEOUT: return "SWIGLU_ERR_DEVICE_TIMEOUT";
+    default: return "SWIGLU_ERR_UNKNOWN";
+  }
+}
+
+const char* swiglu_b200_last_error_message(void) { return t_last_error.c_str(); }
+
+int swiglu_b200_device_status(uint32_t* bits, int clear) {
+  if (!bits) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  uint32_t v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  e = cudaMemcpy(&v, d->status, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status word");
+  if (clear) {
+    e = cudaMemset(d->status, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "clear status word");
+  }
+  *bits = v;
+  return v ? fail(SWIGLU_ERR_DEVICE_TIMEOUT, "kernel pipeline wait timed out (bits 0x%x)", v) : SWIGLU_OK;
+}
+
+int swiglu_b200_fused_matmul_swiglu_save_preact(const void* x, const void* w, void* preact, void* h, int64_t M,
+                                                int64_t K, int64_t H, int dtype, int w_form, int layout,
+                                                int h_from_rounded_preact, int group_size_m, void* stream) {
+  return op_swiglu_fwd(x, w, preact, h, M, K, H, dtype, w_form, layout, h_from_rounded_preact, group_size_m,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout,
+                       int b_layout, int dtype, int out_dtype, int group_size_m, void* stream) {
+  return op_matmul(a, b, c, M, N, K, a_layout, b_layout, dtype, out_dtype, group_size_m,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_bwd_dw2(const void* grad_y, const void* preact, void* dw2, int64_t M, int64_t H, int64_t Dout,
+                        int dtype, int layout, void* stream) {
+  return op_dw2(grad_y, preact, dw2, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_bwd_grad_preact_inplace(const void* grad_y, const void* w2, void* preact, int64_t M, int64_t H,
+                                        int64_t Dout, int dtype, int layout, void* stream) {
+  return op_grad_preact(grad_y, w2, preact, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_forward_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout,
+                              void* stream) {
+  return op_fwd_logic(preact, h, M, H, dtype, layout, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_backward_logic(const void* preact, const void* grad_h, void* grad_preact, int64_t M, int64_t H,
+                               int dtype, int layout, void* stream) {
+  return op_bwd_logic(preact, grad_h, grad_preact, M, H, dtype, layout, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_pack_weight_chunked(const void* src, void* dst, int64_t K, int64_t N_half, int64_t block_n_half,
+                                    int dtype, int unpack, void* stream) {
+  return op_pack(src, dst, K, N_half, block_n_half, dtype, unpack, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_mlp_forward(const void* x, const void* w1, const void* w2, void* preact, void* h_workspace,
+                            void* y, int64_t M, int64_t D, int64_t H, int64_t Dout, int dtype, int w_form,
+                            int layout, int h_from_rounded_preact, void* stream) {
+  if (M > 0 && (!h_workspace || !y || !w2)) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = op_swiglu_fwd(x, w1, preact, h_workspace, M, D, H, dtype, w_form, layout, h_from_rounded_preact, 16,
+                             st))
+    return rc;
+  // y [M, Dout] = h [M, H] . W2^T, W2 stored [Dout, H] (swiglu_recompute.py:65)
+  return op_matmul(h_workspace, w2, y, M, Dout, H, 0, 1, dtype, dtype, 16, st);
+}
+
+int swiglu_b200_mlp_backward(const void* x, const void* w1, const void* w2, void* preact, const void* grad_y,
+                             void* dx, void* dw1, void* dw2, int64_t M, int64_t D, int64_t H, int64_t Dout,
+                             int dtype, int w_form, int layout, void* stream) {
+  if (!w1 || !dw1 || (M > 0 && (!x || !dx))) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (w_form != SWIGLU_W1_ROWS && w_form != SWIGLU_W1_T)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "unknown w_form %d", w_form);
+  if (w_form == SWIGLU_W1_ROWS && layout != SWIGLU_LAYOUT_STD)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "the packed layout applies to the [D, 2H] weight form only");
+  if (int rc = check_dims("mlp_backward", M, D, 2 * H)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // dW2 reads preact, so it runs before grad_preact overwrites it.
+  if (int rc = op_dw2(grad_y, preact, dw2, M, H, Dout, dtype, layout, st)) return rc;
+  if (int rc = op_grad_preact(grad_y, w2, preact, M, H, Dout, dtype, layout, st)) return rc;
+  if (M == 0) {
+    const size_t es = dtype == SWIGLU_F32 ? 4 : 2;
+    cudaError_t e = cudaMemsetAsync(dw1, 0, (size_t)(2 * H * D) * es, st);
+    return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "cudaMemsetAsync(dW1)");
+  }
+  if (w_form == SWIGLU_W1_ROWS) {
+    // grad_W1 [2H, D] = grad_preact^T . x (swiglu_recompute.py:76)
+    if (int rc = op_matmul(preact, x, dw1, 2 * H, D, M, 1, 0, dtype, dtype, 16, st)) return rc;
+    // grad_x [M, D] = grad_preact . W1, W1 stored [2H, D] (swiglu_recompute.py:77)
+    return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 0, dtype, dtype, 16, st);
+  }
+  // grad_wt [D, 2H] = x^T . grad_preact (fused_forward.py:282)
+  if (int rc = op_matmul(x, preact, dw1, D, 2 * H, M, 1, 0, dtype, dtype, 16, st)) return rc;
+  // grad_x [M, D] = grad_preact . wt^T, wt stored [D, 2H] (fused_forward.py:283)
+  return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 1, dtype, dtype, 16, st);
+}
+
+}  // extern "C"

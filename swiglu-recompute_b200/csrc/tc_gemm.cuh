@@ -1,0 +1,477 @@
+// Persistent, warp-specialized tcgen05 GEMM for sm_100a with the SwiGLU
+// prologue/epilogue variants of the recompute MLP.
+//
+//   D[M, N] = A[M, K] * B[K, N]      bf16 operands, f32 accumulation in TMEM
+//
+// Operands are staged in shared memory by TMA with the 128-byte swizzle and
+// consumed by tcgen05.mma straight from shared memory. Each operand may be
+// K-major (K contiguous) or MN-major (M resp. N contiguous); the kernel picks
+// the TMA box orientation and the UMMA descriptor major-ness accordingly, so
+// every transposed GEMM of the backward pass runs without a transpose copy.
+//
+// Warp roles (one CTA per SM, tiles visited in the grouped order of the
+// reference's `_compute_pid`, fused_forward.py:82-94):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue: TMEM -> registers -> epilogue math -> global
+//   warps 6..9  (kTransform only) operand prologue: B <- left * silu(gate)
+//
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Epilogue kinds:
+//   kEpiStore    D -> out0 (bf16 or f32)
+//   kEpiSwiglu   forward GEMM1: tile columns [0,BN/2) are `left`, [BN/2,BN)
+//                `gate` of the same hidden columns; writes preact (left, gate
+//                at their standard or packed positions) and h = left*silu(gate)
+//                (fused_forward.py:101-185, fused_forward_packed.py:129-183)
+//   kEpiDswiglu  backward grad_h GEMM: D = grad_h; reads preact, writes
+//                grad_left / grad_gate over it in place
+//                (swiglu_recompute.py:33-49, fused_forward_packed.py:222-259)
+// kTransform: the B operand is h recomputed from preact in shared memory
+//                (swiglu_recompute.py:71-73 / fused_forward_packed.py:310-311).
+#pragma once
+
+#include "ptx.cuh"
+
+namespace swiglu {
+
+enum EpiKind : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiDswiglu = 2 };
+enum Layout : int { kLayoutStd = 0, kLayoutPacked = 1 };
+
+constexpr int kPackChunk = 128;  // BLOCK_SIZE_N_HALF of the packed layout (fused_forward_packed.py:41)
+
+// Column of `left` / `gate` hidden unit j inside a [.., 2H] preact/weight row.
+// Standard layout: [left | gate]; packed: [left0|gate0|left1|gate1|...] in
+// 128-column chunks (fused_forward_packed.py:77-92).
+__host__ __device__ __forceinline__ int left_col(int j, int H, int layout) {
+  return layout == kLayoutStd ? j : 2 * (j & ~(kPackChunk - 1)) + (j & (kPackChunk - 1));
+}
+__host__ __device__ __forceinline__ int gate_col(int j, int H, int layout) {
+  return layout == kLayoutStd ? H + j : 2 * (j & ~(kPackChunk - 1)) + kPackChunk + (j & (kPackChunk - 1));
+}
+
+struct TcParams {
+  CUtensorMap tmA;  // A operand (box: K-major {64,128} / MN-major {64,64})
+  CUtensorMap tmB;  // B operand, or preact when kTransform (box: K-major {64,BN/2} / MN-major {64,64})
+  void* out0;       // store: D; swiglu: preact; dswiglu: preact (in/out)
+  void* out1;       // swiglu: h (may be null)
+  long long ld0, ld1;
+  int M, N, K;      // N: output columns (swiglu/dswiglu/transform: hidden units)
+  int H;            // hidden width (column maps)
+  int layout;       // kLayoutStd / kLayoutPacked
+  int tiles_m, tiles_n, group_m;
+  int flags;        // kFlagHFromRounded
+  uint32_t mn_lbo;  // MN-major operands: byte offset between 64-element MN blocks
+  uint32_t mn_sbo;  // MN-major operands: byte offset between 8-row K groups
+  uint32_t* status; // device error word
+};
+
+constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
+
+template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool TRANSFORM_, bool OUT_F32_>
+struct TcCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  static constexpr int EPI = EPI_;
+  static constexpr bool TRANSFORM = TRANSFORM_;
+  static constexpr bool OUT_F32 = OUT_F32_;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int G_BYTES = TRANSFORM ? B_BYTES : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + G_BYTES;
+  static constexpr int TX_BYTES = STAGE_BYTES;
+  static constexpr int SMEM_BUDGET = 200 * 1024;
+  static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
+  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int NUM_EPI_WARPS = 4;
+  static constexpr int NUM_XFORM_WARPS = TRANSFORM ? 4 : 0;
+  static constexpr int NUM_THREADS = 32 * (2 + NUM_EPI_WARPS + NUM_XFORM_WARPS);
+  static constexpr int BAR_BYTES = 8 * (4 * STAGES + 5) + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(STAGES >= 2, "pipeline needs at least two stages");
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
+  static_assert(!(TRANSFORM && !B_MN), "the h prologue reads preact rows (MN-major B)");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& pm, int& pn) {
+  // Grouped ordering of output tiles for L2 reuse (fused_forward.py:82-94).
+  const int in_group = group_m * tiles_n;
+  const int gid = tile / in_group;
+  const int first_m = gid * group_m;
+  const int gsz = min(tiles_m - first_m, group_m);
+  const int r = tile % in_group;
+  pm = first_m + r % gsz;
+  pn = r / gsz;
+}
+
+// Store 32 consecutive output columns of one row (cols [c0, c0+32) of a row
+// that starts at `row_ptr`), masking columns >= ncols in groups of 8.
+template <bool F32>
+__device__ __forceinline__ void store_row32(void* row_ptr, int c0, int ncols, const float (&v)[32]) {
+  if constexpr (F32) {
+    float* p = reinterpret_cast<float*>(row_ptr) + c0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      if (c0 + 4 * g + 4 <= ncols) {
+        *reinterpret_cast<float4*>(p + 4 * g) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+      }
+    }
+  } else {
+    __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(row_ptr) + c0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (c0 + 8 * g + 8 <= ncols) {
+        uint4 u;
+        u.x = pack_bf16x2(v[8 * g + 0], v[8 * g + 1]);
+        u.y = pack_bf16x2(v[8 * g + 2], v[8 * g + 3]);
+        u.z = pack_bf16x2(v[8 * g + 4], v[8 * g + 5]);
+        u.w = pack_bf16x2(v[8 * g + 6], v[8 * g + 7]);
+        *reinterpret_cast<uint4*>(p + 8 * g) = u;
+      }
+    }
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled TMA boxes and UMMA atoms need 1024-byte alignment.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;                    // TMA -> (transform | MMA)
+  uint64_t* empty = bars + STAGES;          // MMA -> TMA
+  uint64_t* ready = bars + 2 * STAGES;      // transform -> MMA
+  uint64_t* tmem_full = bars + 3 * STAGES;  // MMA -> epilogue (2)
+  uint64_t* tmem_empty = tmem_full + 2;     // epilogue -> MMA (2)
+  uint64_t* mma_done = tmem_empty + 2;      // MMA teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&ready[s], Cfg::NUM_XFORM_WARPS > 0 ? Cfg::NUM_XFORM_WARPS : 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], Cfg::NUM_EPI_WARPS);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+  uint32_t* status = p.status;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tmA);
+      tma_prefetch_desc(&p.tmB);
+      uint32_t stage = 0, phase = 0;
+      uint32_t filled = 0, fill_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int pm, pn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+        const int m0 = pm * BM;
+        // Origins of the two B halves (BN/2 columns each) and, for the h
+        // prologue, of the two gate halves.
+        int b0, b1, g0 = 0, g1 = 0;
+        if constexpr (Cfg::EPI == kEpiSwiglu) {
+          const int j0 = pn * (BN / 2);
+          b0 = left_col(j0, p.H, p.layout);
+          b1 = gate_col(j0, p.H, p.layout);
+        } else if constexpr (Cfg::TRANSFORM) {
+          const int j0 = pn * BN;
+          b0 = left_col(j0, p.H, p.layout);
+          b1 = b0 + BN / 2;
+          g0 = gate_col(j0, p.H, p.layout);
+          g1 = g0 + BN / 2;
+        } else {
+          b0 = pn * BN;
+          b1 = b0 + BN / 2;
+        }
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          uint8_t* sg = sb + Cfg::B_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::TX_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (Cfg::A_MN) {
+            tma_load_2d(sa, &p.tmA, &full[stage], m0, k0);
+            tma_load_2d(sa + 64 * BK * 2, &p.tmA, &full[stage], m0 + 64, k0);
+          } else {
+            tma_load_2d(sa, &p.tmA, &full[stage], k0, m0);
+          }
+          if constexpr (Cfg::B_MN) {
+#pragma unroll
+            for (int i = 0; i < BN / 128; ++i) {
+              tma_load_2d(sb + i * 8192, &p.tmB, &full[stage], b0 + 64 * i, k0);
+            }
+#pragma unroll
+            for (int i = 0; i < BN / 128; ++i) {
+              tma_load_2d(sb + (BN / 128 + i) * 8192, &p.tmB, &full[stage], b1 + 64 * i, k0);
+            }
+            if constexpr (Cfg::TRANSFORM) {
+#pragma unroll
+              for (int i = 0; i < BN / 128; ++i) tma_load_2d(sg + i * 8192, &p.tmB, &full[stage], g0 + 64 * i, k0);
+#pragma unroll
+              for (int i = 0; i < BN / 128; ++i)
+                tma_load_2d(sg + (BN / 128 + i) * 8192, &p.tmB, &full[stage], g1 + 64 * i, k0);
+            }
+          } else {
+            tma_load_2d(sb, &p.tmB, &full[stage], k0, b0);
+            tma_load_2d(sb + (BN / 2) * 128, &p.tmB, &full[stage], k0, b1);
+          }
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every load this thread issued must land before the CTA exits.
+      for (int s = 0; s < STAGES; ++s) {
+        if (filled & (1u << s)) {
+          volatile int never = 0;
+          mbar_wait(&full[s], (fill_parity >> s) & 1u, &never, status, kErrTimeoutTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          uint64_t* wait_bar = Cfg::TRANSFORM ? &ready[stage] : &full[stage];
+          if (!mbar_wait(wait_bar, phase, abort_flag, status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 16 elements = 32 bytes inside the swizzle row.
+            // MN-major: advance 16 rows of 128 bytes.
+            const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
+                                             : make_smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sb + k * 2048, p.mn_lbo, p.mn_sbo)
+                                             : make_smem_desc_sw128(sb + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // All MMAs issued by this thread complete before TMEM is released.
+      umma_commit(mma_done);
+      volatile int never = 0;
+      mbar_wait(mma_done, 0, &never, status, kErrTimeoutTeardown);
+    }
+  } else if (warp < 2 + Cfg::NUM_EPI_WARPS) {
+    // ------------------------------------------------------------- epilogue
+    const uint32_t q = warp & 3u;  // TMEM lane quarter this warp may access
+    uint32_t acc = 0, acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int pm, pn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
+      tc_fence_after_sync();
+      const int row = pm * BM + static_cast<int>(q * 32 + lane);
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
+
+      if constexpr (Cfg::EPI == kEpiStore) {
+        const int n0 = pn * BN;
+        char* out_row = reinterpret_cast<char*>(p.out0) +
+                        (static_cast<long long>(row) * p.ld0) * (Cfg::OUT_F32 ? 4 : 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          if (row_ok) store_row32<Cfg::OUT_F32>(out_row, n0 + c * 32, p.N, v);
+        }
+      } else if constexpr (Cfg::EPI == kEpiSwiglu) {
+        const int j0 = pn * (BN / 2);
+        __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+        __nv_bfloat16* h_row =
+            p.out1 ? reinterpret_cast<__nv_bfloat16*>(p.out1) + static_cast<long long>(row) * p.ld1 : nullptr;
+        const bool rounded = (p.flags & kFlagHFromRounded) != 0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t rl[32], rg[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, rl);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
+          tmem_ld_wait();
+          const int j = j0 + c * 32;  // first hidden unit of this chunk (multiple of 32)
+          float lf[32], gf[32], hf[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float l = __uint_as_float(rl[i]);
+            float g = __uint_as_float(rg[i]);
+            lf[i] = l;
+            gf[i] = g;
+            if (rounded) {
+              l = bf16_round(l);
+              g = bf16_round(g);
+            }
+            hf[i] = l * (g * sigmoidf_(g));
+          }
+          if (row_ok) {
+            store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
+            store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
+            if (h_row) store_row32<false>(h_row, j, p.N, hf);
+          }
+        }
+      } else {  // kEpiDswiglu
+        const int j0 = pn * BN;
+        __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+          const int j = j0 + c * 32;
+          if (row_ok) {
+          const int lc = left_col(j, p.H, p.layout);
+          const int gc = gate_col(j, p.H, p.layout);
+          float gl[32], gg[32];
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            if (j + 8 * v8 + 8 > p.N) continue;
+            const uint4 lu = *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8);
+            const uint4 gu = *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8);
+            const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+            const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 l2 = unpack_bf16x2(lw[e]);
+              const float2 g2 = unpack_bf16x2(gw[e]);
+              const float ls[2] = {l2.x, l2.y};
+              const float gs[2] = {g2.x, g2.y};
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int i = 8 * v8 + 2 * e + u;
+                // grad_h is a bf16 tensor in the reference before the pointwise step.
+                const float dh = bf16_round(__uint_as_float(r[i]));
+                const float sg = sigmoidf_(gs[u]);
+                const float silu = gs[u] * sg;
+                const float dsilu = sg + silu * (1.0f - sg);
+                gl[i] = dh * silu;
+                gg[i] = dh * ls[u] * dsilu;
+              }
+            }
+          }
+          store_row32<false>(pre_row, lc, lc + (p.N - j), gl);
+          store_row32<false>(pre_row, gc, gc + (p.N - j), gg);
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  } else if constexpr (Cfg::TRANSFORM) {
+    // -------------------------------------------- operand prologue: h tiles
+    // B (left) and G (gate) boxes share one layout, so h is formed element by
+    // element at the same swizzled positions without decoding the swizzle.
+    const uint32_t xt = threadIdx.x - 32 * (2 + Cfg::NUM_EPI_WARPS);
+    constexpr int kChunks = Cfg::B_BYTES / 16;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
+          ok = false;
+          break;
+        }
+        uint4* sb = reinterpret_cast<uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES);
+        const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES +
+                                                         Cfg::B_BYTES);
+#pragma unroll 4
+        for (int i = static_cast<int>(xt); i < kChunks; i += 32 * Cfg::NUM_XFORM_WARPS) {
+          const uint4 lu = sb[i];
+          const uint4 gu = sg[i];
+          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+          uint32_t hw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 l2 = unpack_bf16x2(lw[e]);
+            const float2 g2 = unpack_bf16x2(gw[e]);
+            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoidf_(g2.x)), l2.y * (g2.y * sigmoidf_(g2.y)));
+          }
+          sb[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace swiglu

@@ -1,0 +1,105 @@
+"""ctypes binding of libswiglu_b200.so (the C ABI of include/swiglu_b200.h).
+
+There is no fallback: if the library is missing the first call raises, so a
+machine without the native build can never silently run another code path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from .build import INCLUDE_DIR, LIB_PATH
+
+# Mirrors of the header's enums.
+OK = 0
+F32, BF16 = 0, 1
+LAYOUT_STD, LAYOUT_PACKED128 = 0, 1
+W1_ROWS, W1_T = 0, 1
+
+HEADER = os.path.join(INCLUDE_DIR, "swiglu_b200.h")
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i = ctypes.c_int
+
+# name -> argtypes; restype is int unless listed in _RESTYPES.
+_SIGNATURES = {
+    "swiglu_b200_abi_version": [],
+    "swiglu_b200_status_string": [_i],
+    "swiglu_b200_last_error_message": [],
+    "swiglu_b200_device_status": [ctypes.POINTER(ctypes.c_uint32), _i],
+    "swiglu_b200_fused_matmul_swiglu_save_preact":
+        [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
+    "swiglu_b200_matmul": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
+    "swiglu_b200_bwd_dw2": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_bwd_grad_preact_inplace": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_forward_logic": [_p, _p, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_backward_logic": [_p, _p, _p, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_pack_weight_chunked": [_p, _p, _i64, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_mlp_forward":
+        [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p],
+    "swiglu_b200_mlp_backward":
+        [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i, _i, _p],
+}
+_RESTYPES = {
+    "swiglu_b200_status_string": ctypes.c_char_p,
+    "swiglu_b200_last_error_message": ctypes.c_char_p,
+}
+
+
+class SwigluError(RuntimeError):
+    """A non-zero status from the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_LIB: ctypes.CDLL | None = None
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares."""
+    with open(HEADER) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"\b(swiglu_b200_\w+)\s*\(", text)))
+
+
+def load() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m swiglu_b200.build` "
+            "(from swiglu-recompute_b200/) or __graft_entry__.build(). "
+            "There is no non-native fallback.")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, argtypes in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
+    if lib.swiglu_b200_abi_version() != 1:
+        raise ImportError("libswiglu_b200.so ABI version mismatch")
+    _LIB = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != OK:
+        lib = load()
+        name = lib.swiglu_b200_status_string(status).decode()
+        detail = lib.swiglu_b200_last_error_message().decode()
+        raise SwigluError(status, f"{name}: {detail}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))
+
+
+def device_status(clear: bool = True) -> int:
+    """Timeout bits of the current device's kernels (0 = healthy); synchronises."""
+    bits = ctypes.c_uint32(0)
+    load().swiglu_b200_device_status(ctypes.byref(bits), 1 if clear else 0)
+    return int(bits.value)

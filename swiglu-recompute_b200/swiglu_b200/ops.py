@@ -1,0 +1,178 @@
+"""Tensor-level wrappers over the C ABI.
+
+Each function takes contiguous CUDA tensors, allocates its outputs through the
+torch caching allocator (so `torch.cuda.max_memory_allocated` accounts for
+them, as it does for the reference's `torch.empty` outputs,
+fused_forward.py:216-217), makes the tensors' device current and enqueues the
+native kernels on that device's current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, LAYOUT_PACKED128, LAYOUT_STD, W1_ROWS, W1_T  # noqa: F401
+
+DEFAULT_GROUP_M = 16
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return BF16
+    if dtype == torch.float32:
+        return F32
+    raise TypeError(f"swiglu_b200 supports torch.bfloat16 and torch.float32, got {dtype}")
+
+
+def _p(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(dev: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _check_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("swiglu_b200 kernels take CUDA tensors (there is no CPU path)")
+        if not t.is_contiguous():
+            raise ValueError("swiglu_b200 kernels take contiguous tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def _same_dtype(*ts: torch.Tensor) -> torch.dtype:
+    dt = None
+    for t in ts:
+        if t is None:
+            continue
+        if dt is None:
+            dt = t.dtype
+        elif t.dtype != dt:
+            raise TypeError(f"mixed dtypes {dt} and {t.dtype}")
+    return dt
+
+
+def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
+               h_from_rounded: bool, want_h: bool = True,
+               group_size_m: int = DEFAULT_GROUP_M):
+    """(preact [M, 2H], h [M, H] or None) for preact = x . W1^T in one launch."""
+    dev = _check_cuda(x, w)
+    dt = _same_dtype(x, w)
+    M, K = x.shape
+    if w_form == W1_ROWS:
+        n2, K2 = w.shape
+    else:
+        K2, n2 = w.shape
+    assert K == K2 and n2 % 2 == 0, f"shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}"
+    H = n2 // 2
+    preact = torch.empty((M, n2), device=dev, dtype=dt)
+    h = torch.empty((M, H), device=dev, dtype=dt) if want_h else None
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_fused_matmul_swiglu_save_preact", _p(x), _p(w), _p(preact), _p(h),
+                  M, K, H, dtype_code(dt), w_form, layout, int(bool(h_from_rounded)),
+                  int(group_size_m), _stream(dev))
+    return preact, h
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool, b_t: bool,
+           out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+           group_size_m: int = DEFAULT_GROUP_M) -> torch.Tensor:
+    """C = op(a) . op(b); op(a) = a.T if a_t, op(b) = b.T if b_t."""
+    dev = _check_cuda(a, b, out)
+    dt = _same_dtype(a, b)
+    M, K = (a.shape[1], a.shape[0]) if a_t else tuple(a.shape)
+    Kb, N = (b.shape[1], b.shape[0]) if b_t else tuple(b.shape)
+    assert K == Kb, f"inner dimensions differ: {K} vs {Kb}"
+    odt = out_dtype or dt
+    if out is None:
+        out = torch.empty((M, N), device=dev, dtype=odt)
+    else:
+        assert out.shape == (M, N) and out.dtype == odt
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_matmul", _p(a), _p(b), _p(out), M, N, K, int(a_t), int(b_t),
+                  dtype_code(dt), dtype_code(odt), int(group_size_m), _stream(dev))
+    return out
+
+
+def bwd_dw2(grad_y: torch.Tensor, preact: torch.Tensor, *, layout: int,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """dW2 [Dout, H] = grad_y^T . swiglu(preact), h recomputed in the GEMM prologue."""
+    dev = _check_cuda(grad_y, preact, out)
+    dt = _same_dtype(grad_y, preact)
+    M, Dout = grad_y.shape
+    M2, n2 = preact.shape
+    assert M == M2 and n2 % 2 == 0
+    H = n2 // 2
+    if out is None:
+        out = torch.empty((Dout, H), device=dev, dtype=dt)
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_bwd_dw2", _p(grad_y), _p(preact), _p(out), M, H, Dout,
+                  dtype_code(dt), layout, _stream(dev))
+    return out
+
+
+def bwd_grad_preact_inplace(grad_y: torch.Tensor, w2: torch.Tensor, preact: torch.Tensor, *,
+                            layout: int) -> torch.Tensor:
+    """preact <- grad_preact, from grad_h = grad_y . W2 formed tile by tile (never stored)."""
+    dev = _check_cuda(grad_y, w2, preact)
+    dt = _same_dtype(grad_y, w2, preact)
+    M, Dout = grad_y.shape
+    Dout2, H = w2.shape
+    assert Dout == Dout2 and preact.shape == (M, 2 * H)
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_bwd_grad_preact_inplace", _p(grad_y), _p(w2), _p(preact), M, H, Dout,
+                  dtype_code(dt), layout, _stream(dev))
+    return preact
+
+
+def forward_logic(preact: torch.Tensor, *, layout: int) -> torch.Tensor:
+    dev = _check_cuda(preact)
+    M, n2 = preact.shape
+    assert n2 % 2 == 0
+    H = n2 // 2
+    h = torch.empty((M, H), device=dev, dtype=preact.dtype)
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_forward_logic", _p(preact), _p(h), M, H, dtype_code(preact.dtype),
+                  layout, _stream(dev))
+    return h
+
+
+def backward_logic(preact: torch.Tensor, grad_h: torch.Tensor, *, layout: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _check_cuda(preact, grad_h, out)
+    dt = _same_dtype(preact, grad_h)
+    M, n2 = preact.shape
+    H = n2 // 2
+    assert grad_h.shape == (M, H), f"grad_h {tuple(grad_h.shape)} vs preact {tuple(preact.shape)}"
+    if out is None:
+        out = torch.empty_like(preact)
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_backward_logic", _p(preact), _p(grad_h), _p(out), M, H, dtype_code(dt),
+                  layout, _stream(dev))
+    return out
+
+
+def pack_chunked(w: torch.Tensor, block_n_half: int, *, unpack: bool) -> torch.Tensor:
+    dev = _check_cuda(w)
+    K, n2 = w.shape
+    out = torch.empty_like(w)
+    with torch.cuda.device(dev):
+        _lib.call("swiglu_b200_pack_weight_chunked", _p(w), _p(out), K, n2 // 2, int(block_n_half),
+                  dtype_code(w.dtype), int(bool(unpack)), _stream(dev))
+    return out
+
+
+def device_status(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """Pipeline-timeout bits recorded by the kernels on `device` (0 = healthy)."""
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        return _lib.device_status(clear)

@@ -1,0 +1,261 @@
+"""Tensor-parallel SwiGLU MLP block (Megatron column -> row split, sequence-
+parallel edges) over torch.distributed; NCCL over NVLink on B200.
+
+Rank r of t owns hidden units [r*H/t, (r+1)*H/t):
+  W1 shard  [2H/t, D]  = the left rows AND the gate rows of those units
+                         (left/gate pairs stay on one rank, so SwiGLU is local)
+  W2 shard  [Dout, H/t] = the matching columns of W2
+Tokens are sharded along M: each rank holds x_r [M/t, D] and y_r [M/t, Dout].
+
+forward   x = all_gather(x_r) ; preact_r, h_r = GEMM1+SwiGLU(x, W1_r)
+          y_partial = h_r . W2_r^T (f32) ; y_r = reduce_scatter(y_partial)
+backward  grad_y = all_gather(grad_y_r)
+          dW2_r = grad_y^T . h_r (h recomputed in the GEMM prologue)
+          preact_r <- grad_preact_r (in place) ; dW1_r = grad_preact_r^T . x
+          dx_partial = grad_preact_r . W1_r (f32) ; dx_r = reduce_scatter(dx_partial)
+Partials are reduced in f32 and rounded once, so the result does not depend
+on how many bf16 hops a ring reduction takes.
+
+The reference is single-GPU only; this layer adds the multi-GPU path of the
+benchmark's tensor-parallel configuration (same math per rank as
+SwiGLUMemoryOptimizedFunction, swiglu_recompute.py:58-78).
+"""
+from __future__ import annotations
+
+import os
+import time
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from . import ops
+from .ops import LAYOUT_PACKED128, LAYOUT_STD, W1_ROWS
+
+
+# ------------------------------------------------------------- sharding
+def shard_w1_rows(w1: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Rows of W1 [2H, D] (standard [left; gate]) owned by `rank`: [2H/t, D]."""
+    H = w1.shape[0] // 2
+    assert H % world == 0, f"H={H} must divide evenly over {world} ranks"
+    hs = H // world
+    lo, hi = rank * hs, (rank + 1) * hs
+    return torch.cat([w1[lo:hi], w1[H + lo:H + hi]], dim=0).contiguous()
+
+
+def shard_w2(w2: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Columns of W2 [Dout, H] owned by `rank`: [Dout, H/t]."""
+    H = w2.shape[1]
+    assert H % world == 0
+    hs = H // world
+    return w2[:, rank * hs:(rank + 1) * hs].contiguous()
+
+
+def unshard_w1_rows(shards: list[torch.Tensor]) -> torch.Tensor:
+    """Inverse of shard_w1_rows over all ranks' shards."""
+    hs = shards[0].shape[0] // 2
+    return torch.cat([s[:hs] for s in shards] + [s[hs:] for s in shards], dim=0)
+
+
+# ---------------------------------------------------------- collectives
+def all_gather_rows(t: torch.Tensor, group=None) -> torch.Tensor:
+    world = dist.get_world_size(group)
+    out = torch.empty((t.shape[0] * world, *t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    return out
+
+
+def reduce_scatter_rows(t: torch.Tensor, group=None) -> torch.Tensor:
+    world = dist.get_world_size(group)
+    assert t.shape[0] % world == 0
+    out = torch.empty((t.shape[0] // world, *t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.reduce_scatter_tensor(out, t.contiguous(), group=group)
+    return out
+
+
+# -------------------------------------------------------- local compute
+class NativeCompute:
+    """Per-rank compute on libswiglu_b200.so (bf16 tcgen05 or f32 kernels)."""
+
+    @staticmethod
+    def swiglu_fwd(x, w1_local):
+        return ops.swiglu_fwd(x, w1_local, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+
+    @staticmethod
+    def matmul(a, b, *, a_t, b_t, out_dtype=None):
+        return ops.matmul(a, b, a_t=a_t, b_t=b_t, out_dtype=out_dtype)
+
+    @staticmethod
+    def dw2(gy, preact):
+        return ops.bwd_dw2(gy, preact, layout=LAYOUT_STD)
+
+    @staticmethod
+    def grad_preact_inplace(gy, w2_local, preact):
+        return ops.bwd_grad_preact_inplace(gy, w2_local, preact, layout=LAYOUT_STD)
+
+
+class _TPSwiGLUFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32):
+        x = all_gather_rows(x_local, group)
+        preact, h = compute.swiglu_fwd(x, w1_local)
+        acc_dt = torch.float32 if reduce_f32 else x.dtype
+        y_part = compute.matmul(h, w2_local, a_t=False, b_t=True, out_dtype=acc_dt)
+        del h
+        y_local = reduce_scatter_rows(y_part, group).to(x.dtype)
+        ctx.save_for_backward(x, w1_local, w2_local, preact)
+        ctx.group, ctx.compute, ctx.reduce_f32 = group, compute, reduce_f32
+        return y_local
+
+    @staticmethod
+    def backward(ctx, grad_y_local):
+        if getattr(ctx, "_consumed", False):
+            raise RuntimeError("tensor-parallel SwiGLU backward already consumed its saved preact")
+        ctx._consumed = True
+        x, w1_local, w2_local, preact = ctx.saved_tensors
+        compute = ctx.compute
+        gy = all_gather_rows(grad_y_local.to(x.dtype), ctx.group)
+        dw2 = compute.dw2(gy, preact)
+        gp = compute.grad_preact_inplace(gy, w2_local, preact)
+        torch.autograd.graph.increment_version(preact)
+        dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
+        acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
+        dx_part = compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt)
+        dx_local = reduce_scatter_rows(dx_part, ctx.group).to(x.dtype)
+        return dx_local, dw1, dw2, None, None, None
+
+
+def tp_swiglu(x_local, w1_local, w2_local, group=None, compute=NativeCompute, reduce_f32=True):
+    """y_r [M/t, Dout] for the token shard x_r [M/t, D]; see the module docstring."""
+    return _TPSwiGLUFunction.apply(x_local, w1_local, w2_local, group, compute, reduce_f32)
+
+
+class SwiGLUMLPTensorParallel(nn.Module):
+    """One SwiGLU MLP block split over the ranks of `group` (weights are this
+    rank's shards: w1 [2H/t, D], w2 [Dout, H/t])."""
+
+    def __init__(self, dim, hidden_dim, out_dim=None, dtype=torch.float32, group=None,
+                 reduce_f32=True):
+        super().__init__()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        assert hidden_dim % self.world == 0
+        self.dim, self.hidden_dim = dim, hidden_dim
+        self.out_dim = out_dim if out_dim is not None else dim
+        self.reduce_f32 = reduce_f32
+        hs = hidden_dim // self.world
+        self.w1 = nn.Parameter(torch.empty(2 * hs, dim, dtype=dtype))
+        self.w2 = nn.Parameter(torch.empty(self.out_dim, hs, dtype=dtype))
+
+    @torch.no_grad()
+    def load_full(self, w1: torch.Tensor, w2: torch.Tensor):
+        self.w1.copy_(shard_w1_rows(w1, self.rank, self.world))
+        self.w2.copy_(shard_w2(w2, self.rank, self.world))
+        return self
+
+    def forward(self, x_local):
+        return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32)
+
+
+# -------------------------------------------------------------- bench
+def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
+    """Strong-scaling TP run of the config-2 block on WORLD_SIZE GPUs (one
+    process per GPU). Returns the JSON dict on rank 0, None elsewhere."""
+    from oracle.swiglu_oracle import make_inputs
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+    try:
+        M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
+        assert M % world == 0 and H % world == 0
+        x, w1, w2, gy = make_inputs(M, D, H, Dout, seed=0, dtype=torch.bfloat16)
+        ms_rows = M // world
+        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16).to(dev).load_full(w1, w2)
+        params = list(model.parameters())
+        x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
+        gy_l = gy[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
+        del x, w1, w2, gy
+
+        def step():
+            xi = x_l.detach().requires_grad_(True)
+            y = model(xi)
+            return torch.autograd.grad(y, [xi] + params, gy_l)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with clock_cls(local) as clk:
+            time.sleep(0.3)
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(st)
+            for _ in range(args.steps):
+                step()
+            e1.record(st)
+            torch.cuda.synchronize()
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+
+        # End to end with host buffers: this rank's token shard in, its grad_x out.
+        x_h, gy_h = x_l.cpu().pin_memory(), gy_l.cpu().pin_memory()
+        dx_h = torch.empty_like(x_h).pin_memory()
+
+        def e2e_step():
+            xi = x_h.to(dev, non_blocking=True).requires_grad_(True)
+            gyi = gy_h.to(dev, non_blocking=True)
+            y = model(xi)
+            gx = torch.autograd.grad(y, [xi] + params, gyi)[0]
+            dx_h.copy_(gx, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(st)
+        for _ in range(args.steps):
+            e2e_step()
+        e3.record(st)
+        torch.cuda.synchronize()
+        e2e_ms = torch.tensor([e2.elapsed_time(e3) / args.steps], device=dev)
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        e2e_ms = e2e_ms.item()
+        status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
+        dist.all_reduce(status, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        if rank != 0:
+            return None
+        fl = flops_fn(M, D, H, Dout)
+        peaks, src = load_peaks()
+        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        value = fl / (ms * 1e-3) / 1e12
+        return {
+            "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "cfg2: one SwiGLU MLP block fwd+bwd, tensor parallel", **cfg,
+                       "parallelism": f"tp{world}", "reduce": "f32 partials, NCCL reduce-scatter",
+                       "l2": "working set > L2"},
+            "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": 2 * x_h.numel() * 2 * world,
+                    "d2h_bytes_per_step": dx_h.numel() * 2 * world},
+            "gpu_launches": 6 * args.steps * world,
+            "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
+            "device_status": int(status.item()),
+            "clocks": clk.summary(),
+        }
+    finally:
+        dist.destroy_process_group()

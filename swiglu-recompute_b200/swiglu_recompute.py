@@ -1,0 +1,164 @@
+"""SwiGLU MLP with backward-pass recomputation of the activation `h` (B200 build).
+
+Drop-in for the reference module of the same name
+(tongzhou8086/swiglu-recompute, swiglu_recompute.py): same symbols, same
+signatures, same saved state. The forward saves `preact = x @ W1.t()` but not
+`h = left * silu(gate)`; the backward recomputes `h` and the SiLU factors from
+`preact`.
+
+What runs underneath is libswiglu_b200.so (hand-written sm_100a kernels):
+  forward   one tcgen05 GEMM whose epilogue writes preact and h
+            (h from the bf16-rounded preact, as swiglu_recompute.py:64 does),
+            then y = h @ W2.t() on tcgen05; h is a transient buffer.
+  backward  dW2 = grad_y.t() @ h with h recomputed in the GEMM operand prologue;
+            grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
+            written over preact in place (no [M, H] temporaries, no cat);
+            dW1 = grad_preact.t() @ x and dx = grad_preact @ W1 on tcgen05.
+fp32 inputs run the same dataflow on fp32 FFMA kernels (correctness mode).
+
+Shapes:  x [M, D]   W1 [2H, D]   W2 [Dout, H]
+         preact [M, 2H]   h [M, H]   y [M, Dout]
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from swiglu_b200 import ops
+from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+
+
+# -----------------------------------------------------------------------------
+# Core SwiGLU math helpers (swiglu_recompute.py:26-49): native pointwise kernels
+# -----------------------------------------------------------------------------
+def _swiglu_forward_logic(preact: torch.Tensor) -> torch.Tensor:
+    """h = left * silu(gate), from preact [M, 2H] -> h [M, H]."""
+    shape = preact.shape
+    p2 = preact.reshape(-1, shape[-1]).contiguous()
+    h = ops.forward_logic(p2, layout=LAYOUT_STD)
+    return h.reshape(*shape[:-1], shape[-1] // 2)
+
+
+def _swiglu_backward_logic(preact: torch.Tensor, grad_h: torch.Tensor) -> torch.Tensor:
+    """grad_preact [M, 2H] from preact and grad_h [M, H], via the explicit SiLU derivative.
+
+    silu'(z) = sigmoid(z) + silu(z) * (1 - sigmoid(z))
+    grad_left = grad_h * silu(gate)
+    grad_gate = grad_h * left * silu'(gate)
+    """
+    shape = preact.shape
+    p2 = preact.reshape(-1, shape[-1]).contiguous()
+    g2 = grad_h.reshape(-1, grad_h.shape[-1]).contiguous()
+    return ops.backward_logic(p2, g2, layout=LAYOUT_STD).reshape(shape)
+
+
+def _flatten_rows(x: torch.Tensor) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    return x2 if x2.is_contiguous() else x2.contiguous()
+
+
+def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
+    """Shared backward of the three recompute Functions.
+
+    Order matters: dW2 reads preact, the grad_h GEMM then overwrites preact
+    with grad_preact, and dW1 / dx read grad_preact. preact is internal to the
+    Function (never a graph output), so consuming it is safe; its version
+    counter is bumped so that a second backward through the same graph raises
+    instead of reading grad_preact as preact.
+    """
+    if getattr(ctx, "_preact_consumed", False):
+        raise RuntimeError(
+            "SwiGLU recompute backward was already run for this graph: the saved preact "
+            "was consumed in place (retain_graph / double backward is not supported)")
+    need_x, need_w1, need_w2 = ctx.needs_input_grad[:3]
+    gy = _flatten_rows(grad_y)
+    if gy.dtype != preact.dtype:
+        gy = gy.to(preact.dtype)
+    grad_w2 = ops.bwd_dw2(gy, preact, layout=layout) if need_w2 else None
+    grad_x = grad_w1 = None
+    if need_x or need_w1:
+        ctx._preact_consumed = True
+        gp = ops.bwd_grad_preact_inplace(gy, w2, preact, layout=layout)
+        torch.autograd.graph.increment_version(preact)
+        if need_w1:
+            if w_form == W1_ROWS:
+                grad_w1 = ops.matmul(gp, x, a_t=True, b_t=False)      # [2H, D] = gp^T x
+            else:
+                grad_w1 = ops.matmul(x, gp, a_t=True, b_t=False)      # [D, 2H] = x^T gp
+        if need_x:
+            grad_x = ops.matmul(gp, w1, a_t=False, b_t=(w_form != W1_ROWS))
+    return grad_x, grad_w1, grad_w2
+
+
+# -----------------------------------------------------------------------------
+# Custom autograd.Function: recompute `h` in backward instead of saving it.
+# -----------------------------------------------------------------------------
+class SwiGLUMemoryOptimizedFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, W1, W2):
+        lead = x.shape[:-1]
+        x2 = _flatten_rows(x)
+        W1c, W2c = W1.contiguous(), W2.contiguous()
+        # preact [M, 2H] and the transient h [M, H] from one tcgen05 launch.
+        preact, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+        y = ops.matmul(h, W2c, a_t=False, b_t=True)            # [M, Dout] = h W2^T
+        del h                                                 # h is NOT retained
+        ctx.save_for_backward(x2, W1c, W2c, preact)
+        ctx.x_shape = x.shape
+        return y.reshape(*lead, W2.shape[0])
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        x, W1, W2, preact = ctx.saved_tensors
+        gx, gw1, gw2 = _recompute_backward(ctx, grad_y, x, W1, W2, preact,
+                                           w_form=W1_ROWS, layout=LAYOUT_STD)
+        if gx is not None:
+            gx = gx.reshape(ctx.x_shape)
+        return gx, gw1, gw2
+
+
+# -----------------------------------------------------------------------------
+# nn.Module wrapper
+# -----------------------------------------------------------------------------
+class SwiGLUMLPCustom(nn.Module):
+    """SwiGLU MLP (dim -> hidden -> out_dim) using backward recomputation of `h`."""
+
+    def __init__(self, dim, hidden_dim, out_dim=None, dtype=torch.float32):
+        super().__init__()
+        self.dim = dim
+        self.hidden_dim = hidden_dim
+        self.out_dim = out_dim if out_dim is not None else dim
+        self.w1 = nn.Parameter(torch.empty(2 * hidden_dim, dim, dtype=dtype))
+        self.w2 = nn.Parameter(torch.empty(self.out_dim, hidden_dim, dtype=dtype))
+        nn.init.xavier_uniform_(self.w1)
+        nn.init.xavier_uniform_(self.w2)
+
+    def forward(self, x):
+        return SwiGLUMemoryOptimizedFunction.apply(x, self.w1, self.w2)
+
+
+class SwiGLUMLPGroundTruth(nn.Module):
+    """Standard SwiGLU MLP relying on PyTorch autograd (saves `h` and `preact`).
+
+    This is the reference's ground-truth model (swiglu_recompute.py:101-118),
+    kept as plain PyTorch on purpose: it is the comparison target of the
+    parity checks, not part of the native path.
+    """
+
+    def __init__(self, dim, hidden_dim, out_dim=None, dtype=torch.float32):
+        super().__init__()
+        self.dim = dim
+        self.hidden_dim = hidden_dim
+        self.out_dim = out_dim if out_dim is not None else dim
+        self.w1 = nn.Parameter(torch.empty(2 * hidden_dim, dim, dtype=dtype))
+        self.w2 = nn.Parameter(torch.empty(self.out_dim, hidden_dim, dtype=dtype))
+        nn.init.xavier_uniform_(self.w1)
+        nn.init.xavier_uniform_(self.w2)
+
+    def forward(self, x):
+        preact = x @ self.w1.t()
+        left, gate = preact.chunk(2, dim=-1)
+        h = left * F.silu(gate)
+        return h @ self.w2.t()

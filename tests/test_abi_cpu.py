@@ -1,0 +1,76 @@
+"""The C-ABI library: loads without a GPU, exports every header symbol, and
+rejects bad arguments before touching the device. CPU only (no compute calls)."""
+import ctypes
+
+import pytest
+
+from swiglu_b200 import _lib
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def test_exports_every_header_symbol(lib):
+    syms = _lib.header_symbols()
+    assert len(syms) >= 13
+    for s in syms:
+        assert hasattr(lib, s), s
+    # Every declared symbol has a binding signature (no unbound entry points).
+    assert set(syms) == set(_lib._SIGNATURES)
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.swiglu_b200_abi_version() == 1
+    assert lib.swiglu_b200_status_string(0) == b"SWIGLU_OK"
+    assert lib.swiglu_b200_status_string(1) == b"SWIGLU_ERR_INVALID_ARGUMENT"
+    assert lib.swiglu_b200_status_string(5) == b"SWIGLU_ERR_DEVICE_TIMEOUT"
+    assert lib.swiglu_b200_status_string(99) == b"SWIGLU_ERR_UNKNOWN"
+
+
+def _p(v):
+    return ctypes.c_void_p(v)
+
+
+@pytest.mark.parametrize("args,fragment", [
+    # unknown dtype
+    ((_p(16), _p(16), _p(16), 8, 8, 8, 0, 0, 7, 1, 16, _p(0)), b"dtype"),
+    # bad layout flag
+    ((_p(16), _p(16), _p(16), 8, 8, 8, 2, 0, 1, 1, 16, _p(0)), b"layout"),
+    # null pointer
+    ((_p(0), _p(16), _p(16), 8, 8, 8, 0, 0, 1, 1, 16, _p(0)), b"null"),
+    # K = 0
+    ((_p(16), _p(16), _p(16), 8, 8, 0, 0, 0, 1, 1, 16, _p(0)), b"K must be positive"),
+    # f32 GEMM cannot write bf16
+    ((_p(16), _p(16), _p(16), 8, 8, 8, 0, 0, 0, 1, 16, _p(0)), b"f32"),
+    # negative size
+    ((_p(16), _p(16), _p(16), -1, 8, 8, 0, 0, 1, 1, 16, _p(0)), b"dimensions"),
+])
+def test_matmul_rejects_bad_arguments(lib, args, fragment):
+    rc = lib.swiglu_b200_matmul(*args)
+    assert rc == 1
+    assert fragment in lib.swiglu_b200_last_error_message()
+
+
+def test_swiglu_forward_argument_checks(lib):
+    f = lib.swiglu_b200_fused_matmul_swiglu_save_preact
+    # packed layout needs H % 128 == 0
+    assert f(_p(16), _p(16), _p(16), _p(0), 128, 64, 96, 1, 1, 1, 0, 16, _p(0)) == 1
+    assert b"128" in lib.swiglu_b200_last_error_message()
+    # packed layout only with the [D, 2H] weight form
+    assert f(_p(16), _p(16), _p(16), _p(0), 128, 64, 128, 1, 0, 1, 0, 16, _p(0)) == 1
+    # group size must be positive
+    assert f(_p(16), _p(16), _p(16), _p(0), 128, 64, 128, 1, 1, 0, 0, 0, _p(0)) == 1
+
+
+def test_pack_rejects_alias_and_bad_block(lib):
+    f = lib.swiglu_b200_pack_weight_chunked
+    assert f(_p(16), _p(16), 4, 256, 128, 1, 0, _p(0)) == 1
+    assert f(_p(16), _p(32), 4, 250, 128, 1, 0, _p(0)) == 1
+
+
+def test_check_raises_with_detail(lib):
+    rc = lib.swiglu_b200_bwd_dw2(_p(0), _p(16), _p(16), 8, 8, 8, 1, 0, _p(0))
+    with pytest.raises(_lib.SwigluError, match="SWIGLU_ERR_INVALID_ARGUMENT: null pointer"):
+        _lib.check(rc)

@@ -1,0 +1,144 @@
+"""Each native entry point against the CPU oracle on the same seeded inputs.
+
+GPU only. bf16 results are compared with a CPU fp32 computation from the same
+bf16 values, rounded to bf16 at the points the reference rounds; the bound is
+rel_max <= 8e-3 (one bf16 ulp is 2^-8 = 3.9e-3 of the element; rel_max is
+relative to the largest element). f32 results: rel_max <= 1e-5.
+"""
+import pytest
+import torch
+
+from oracle import swiglu_oracle as O
+from swiglu_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 8e-3
+F32_TOL = 1e-5
+DEV = "cuda"
+
+
+def _r(*shape, seed=0, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype)
+
+
+def _tol(dtype):
+    return BF16_TOL if dtype == torch.bfloat16 else F32_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 264, 136), (128, 256, 64), (384, 768, 1024)])
+def test_matmul_layouts(dtype, a_t, b_t, M, N, K):
+    if a_t and M % 8:
+        pytest.skip("MN-major A needs M % 8 == 0")
+    a = _r(*((K, M) if a_t else (M, K)), seed=1, dtype=dtype)
+    b = _r(*((N, K) if b_t else (K, N)), seed=2, scale=K ** -0.5, dtype=dtype)
+    ref = (a.float().t() if a_t else a.float()) @ (b.float().t() if b_t else b.float())
+    out = ops.matmul(a.to(DEV), b.to(DEV), a_t=a_t, b_t=b_t)
+    assert out.dtype == dtype
+    assert O.rel_max(out.cpu(), ref) <= _tol(dtype)
+
+
+def test_matmul_f32_output_of_bf16_gemm():
+    a, b = _r(256, 512, seed=3), _r(512, 256, seed=4, scale=512 ** -0.5)
+    ref = a.float() @ b.float()
+    out = ops.matmul(a.to(DEV), b.to(DEV), a_t=False, b_t=False, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    assert O.rel_max(out.cpu(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("form,layout", [(ops.W1_ROWS, O.STD), (ops.W1_T, O.STD), (ops.W1_T, O.PACKED)])
+@pytest.mark.parametrize("rounded", [False, True])
+@pytest.mark.parametrize("M,K,H", [(256, 256, 256), (200, 136, 384), (128, 64, 128)])
+def test_swiglu_forward_epilogue(dtype, form, layout, rounded, M, K, H):
+    if layout == O.PACKED and H % 128:
+        pytest.skip("packed layout needs H % 128 == 0")
+    x = _r(M, K, seed=5, dtype=dtype)
+    w_rows_std = _r(2 * H, K, seed=6, scale=K ** -0.5, dtype=dtype)          # [left; gate] rows
+    li, gi = O.col_index(H, layout)
+    w_rows = torch.empty_like(w_rows_std)
+    w_rows[li] = w_rows_std[:H]
+    w_rows[gi] = w_rows_std[H:]
+    w = w_rows if form == ops.W1_ROWS else w_rows.t().contiguous()
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    preact, h = ops.swiglu_fwd(x.to(DEV), w.to(DEV), w_form=form, layout=lay, h_from_rounded=rounded)
+    bf = dtype == torch.bfloat16
+    acc = x.float() @ w_rows.float().t()
+    ref_pre = O._round(acc, bf)
+    ref_h = O.forward_logic(ref_pre if (rounded and bf) else acc, layout, bf)
+    assert O.rel_max(preact.cpu(), ref_pre) <= _tol(dtype)
+    assert O.rel_max(h.cpu(), ref_h) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("layout", [O.STD, O.PACKED])
+@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (1000, 128, 256)])
+def test_dw2_with_recomputed_h(dtype, layout, M, H, Dout):
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    gy = _r(M, Dout, seed=7, dtype=dtype)
+    preact = _r(M, 2 * H, seed=8, dtype=dtype)
+    bf = dtype == torch.bfloat16
+    h = O.forward_logic(preact.float(), layout, bf)
+    ref = gy.float().t() @ h
+    out = ops.bwd_dw2(gy.to(DEV), preact.to(DEV), layout=lay)
+    assert O.rel_max(out.cpu(), ref) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("layout", [O.STD, O.PACKED])
+@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (128, 640, 64)])
+def test_grad_preact_inplace(dtype, layout, M, H, Dout):
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    gy = _r(M, Dout, seed=9, dtype=dtype)
+    w2 = _r(Dout, H, seed=10, scale=H ** -0.5, dtype=dtype)
+    preact = _r(M, 2 * H, seed=11, dtype=dtype)
+    bf = dtype == torch.bfloat16
+    grad_h = O._round(gy.float() @ w2.float(), bf)
+    ref = O.backward_logic(preact.float(), grad_h, layout, bf)
+    p_dev = preact.to(DEV)
+    ptr = p_dev.data_ptr()
+    out = ops.bwd_grad_preact_inplace(gy.to(DEV), w2.to(DEV), p_dev, layout=lay)
+    assert out.data_ptr() == ptr
+    assert O.rel_max(p_dev.cpu(), ref) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("layout", [O.STD, O.PACKED])
+def test_pointwise_kernels(dtype, layout):
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    M, H = 300, 512
+    preact = _r(M, 2 * H, seed=12, dtype=dtype)
+    gh = _r(M, H, seed=13, dtype=dtype)
+    bf = dtype == torch.bfloat16
+    h = ops.forward_logic(preact.to(DEV), layout=lay)
+    assert O.rel_max(h.cpu(), O.forward_logic(preact, layout, bf)) <= _tol(dtype)
+    gp = ops.backward_logic(preact.to(DEV), gh.to(DEV), layout=lay)
+    assert O.rel_max(gp.cpu(), O.backward_logic(preact, gh, layout, bf)) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("block", [128, 64, 32])
+def test_pack_unpack_exact(dtype, block):
+    w = _r(48, 2 * 256, seed=14, dtype=dtype)
+    pk = ops.pack_chunked(w.to(DEV), block, unpack=False)
+    assert torch.equal(pk.cpu(), O.pack_weight_chunked(w, block))
+    assert torch.equal(ops.pack_chunked(pk, block, unpack=True).cpu(), w)
+
+
+def test_empty_batch_is_a_no_op_with_zero_weight_grads():
+    H, D, Dout = 128, 64, 64
+    x = torch.empty(0, D, dtype=torch.bfloat16, device=DEV)
+    w1 = _r(2 * H, D, seed=15).to(DEV)
+    preact, h = ops.swiglu_fwd(x, w1, w_form=ops.W1_ROWS, layout=ops.LAYOUT_STD, h_from_rounded=True)
+    assert preact.shape == (0, 2 * H) and h.shape == (0, H)
+    gy = torch.empty(0, Dout, dtype=torch.bfloat16, device=DEV)
+    dw2 = ops.bwd_dw2(gy, preact, layout=ops.LAYOUT_STD)
+    assert dw2.shape == (Dout, H) and dw2.abs().max().item() == 0.0
+
+
+def test_device_status_healthy_after_all_kernels():
+    assert ops.device_status(0) == 0

@@ -1,0 +1,125 @@
+"""Tensor-parallel host logic on CPU: sharding, all-gather / reduce-scatter
+placement and the backward order, run as world_size-2 gloo ranks with the
+oracle's math standing in for the per-rank CUDA kernels. CPU only."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import swiglu_oracle as O
+from swiglu_b200 import tp
+
+
+class OracleCompute:
+    """Per-rank compute with the oracle's f32 math (test stand-in for NativeCompute)."""
+
+    @staticmethod
+    def swiglu_fwd(x, w1_local):
+        preact = x @ w1_local.t()
+        return preact, O.forward_logic(preact)
+
+    @staticmethod
+    def matmul(a, b, *, a_t, b_t, out_dtype=None):
+        out = (a.t() if a_t else a) @ (b.t() if b_t else b)
+        return out.to(out_dtype) if out_dtype is not None else out
+
+    @staticmethod
+    def dw2(gy, preact):
+        return gy.t() @ O.forward_logic(preact)
+
+    @staticmethod
+    def grad_preact_inplace(gy, w2_local, preact):
+        preact.copy_(O.backward_logic(preact, gy @ w2_local))
+        return preact
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, M, D, H, Dout, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.set_num_threads(1)
+        x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=3)
+        ms = M // world
+        w1_l = tp.shard_w1_rows(w1, rank, world).requires_grad_(True)
+        w2_l = tp.shard_w2(w2, rank, world).requires_grad_(True)
+        x_l = x[rank * ms:(rank + 1) * ms].clone().requires_grad_(True)
+        y_l = tp.tp_swiglu(x_l, w1_l, w2_l, None, OracleCompute, True)
+        dx_l, dw1_l, dw2_l = torch.autograd.grad(y_l, [x_l, w1_l, w2_l], gy[rank * ms:(rank + 1) * ms])
+        q.put((rank, y_l.detach(), dx_l, dw1_l, dw2_l))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_matches_single_rank_oracle(world):
+    M, D, H, Dout = 64, 48, 128, 40
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, H, Dout, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=3)
+    ref = O.mlp_forward_backward(x, w1, w2, gy)
+    y = torch.cat([r[1] for r in res])
+    dx = torch.cat([r[2] for r in res])
+    dw1 = tp.unshard_w1_rows([r[3] for r in res])
+    dw2 = torch.cat([r[4] for r in res], dim=1)
+    assert O.rel_max(y, ref["y"]) <= 1e-5
+    assert O.rel_max(dx, ref["dx"]) <= 1e-5
+    assert O.rel_max(dw1, ref["dw1"]) <= 1e-5
+    assert O.rel_max(dw2, ref["dw2"]) <= 1e-5
+
+
+def test_shard_roundtrip():
+    w1 = torch.randn(2 * 256, 32)
+    shards = [tp.shard_w1_rows(w1, r, 4) for r in range(4)]
+    assert all(s.shape == (128, 32) for s in shards)
+    assert torch.equal(tp.unshard_w1_rows(shards), w1)
+    # each shard holds left AND gate rows of the same hidden units
+    assert torch.equal(shards[1][:64], w1[64:128])
+    assert torch.equal(shards[1][64:], w1[256 + 64:256 + 128])
+    w2 = torch.randn(16, 256)
+    assert torch.equal(torch.cat([tp.shard_w2(w2, r, 4) for r in range(4)], dim=1), w2)
+
+
+def _dying_worker(rank, world, port, q):
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)          # a rank that dies between steps
+    try:
+        t = torch.ones(4, 2)
+        tp.all_gather_rows(t)
+        q.put("no error")
+    except Exception as e:   # the survivor sees an error, not a hang
+        q.put(type(e).__name__)
+
+
+def test_dead_rank_surfaces_as_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert msg != "no error"
