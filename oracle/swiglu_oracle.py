@@ -120,6 +120,22 @@ def mlp_forward_backward(x, w1_rows, w2, grad_y, *, bf16: bool = False,
     return {"y": y, "dx": dx, "dw1": dw1, "dw2": dw2, "preact": preact, "h": h}
 
 
+def reference_path_bf16(x, w1_rows, w2, grad_y):
+    """The recompute Function's own bf16 arithmetic, op for op
+    (swiglu_recompute.py:58-78): bf16 x bf16 -> bf16 matmuls (f32
+    accumulation in the BLAS of whatever device the tensors live on) and the
+    pointwise helpers in f32 rounded once. Run on CUDA tensors it reproduces
+    what the reference computes on the GPU; the parity tests use it there."""
+    x, w1, w2, gy = (t.to(torch.bfloat16) for t in (x, w1_rows, w2, grad_y))
+    preact = x @ w1.t()
+    h = forward_logic(preact.float(), STD, True).to(torch.bfloat16)
+    y = h @ w2.t()
+    dw2 = gy.t() @ h
+    grad_h = gy @ w2
+    gp = backward_logic(preact.float(), grad_h.float(), STD, True).to(torch.bfloat16)
+    return {"y": y, "dx": gp @ w1, "dw1": gp.t() @ x, "dw2": dw2}
+
+
 def ground_truth(x, w1, w2, grad_y):
     """Autograd through the standard MLP (SwiGLUMLPGroundTruth, swiglu_recompute.py:101-118)."""
     x = x.detach().clone().requires_grad_(True)

@@ -12,6 +12,7 @@
 #include <string>
 
 #include "simt_kernels.cuh"
+#include "tc_dw2.cuh"
 
 namespace swiglu {
 
@@ -285,8 +286,8 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   p.flags = rounded ? kFlagHFromRounded : 0;
   if (reinterpret_cast<uintptr_t>(preact) % 16 || (h && reinterpret_cast<uintptr_t>(h) % 16))
     return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
-  return w_form == SWIGLU_W1_ROWS ? launch_tc<TcCfg<256, false, false, kEpiSwiglu, false, false>>(p, *d, st)
-                                  : launch_tc<TcCfg<256, false, true, kEpiSwiglu, false, false>>(p, *d, st);
+  return w_form == SWIGLU_W1_ROWS ? launch_tc<TcCfg<256, false, false, kEpiSwiglu, false>>(p, *d, st)
+                                  : launch_tc<TcCfg<256, false, true, kEpiSwiglu, false>>(p, *d, st);
 }
 
 int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout, int b_layout,
@@ -345,7 +346,7 @@ int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64
   p.tiles_n = (int)((N + 255) / 256);
   p.group_m = group_m;
   const bool f32 = out_dtype == SWIGLU_F32;
-#define SWIGLU_MM(AM, BM_, F) launch_tc<TcCfg<256, AM, BM_, kEpiStore, false, F>>(p, *d, st)
+#define SWIGLU_MM(AM, BM_, F) launch_tc<TcCfg<256, AM, BM_, kEpiStore, F>>(p, *d, st)
   if (f32) {
     if (a_mn) return b_mn ? SWIGLU_MM(true, true, true) : SWIGLU_MM(true, false, true);
     return b_mn ? SWIGLU_MM(false, true, true) : SWIGLU_MM(false, false, true);
@@ -381,17 +382,29 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   }
   if (int rc = check_mult8("H", H)) return rc;
   if (int rc = check_mult8("Dout", Dout)) return rc;
-  TcParams p{};
-  if (int rc = map_mnmajor(&p.tmA, gy, M, Dout, Dout, "grad_y")) return rc;
-  if (int rc = map_mnmajor(&p.tmB, preact, M, 2 * H, 2 * H, "preact")) return rc;
+  Dw2Params p{};
+  if (int rc = make_map(&p.tm_pre, preact, 2 * H, M, 2 * H, Dw2Cfg::BK, "preact")) return rc;
+  if (int rc = make_map(&p.tm_gy, gy, Dout, M, Dout, Dw2Cfg::BK, "grad_y")) return rc;
   if (reinterpret_cast<uintptr_t>(dw2) % 16) return fail(SWIGLU_ERR_MISALIGNED, "dW2 must be 16-byte aligned");
-  p.out0 = dw2;
-  p.ld0 = H;
-  p.M = (int)Dout, p.N = (int)H, p.K = (int)M, p.H = (int)H, p.layout = layout;
-  p.tiles_m = (int)((Dout + 127) / 128);
-  p.tiles_n = (int)((H + 127) / 128);
-  p.group_m = 8;
-  return launch_tc<TcCfg<128, true, true, kEpiStore, true, false>>(p, *d, st);
+  p.dw2 = static_cast<__nv_bfloat16*>(dw2);
+  p.M = (int)M, p.H = (int)H, p.Dout = (int)Dout, p.layout = layout;
+  p.tiles_j = (int)((H + Dw2Cfg::BJ - 1) / Dw2Cfg::BJ);
+  p.tiles_d = (int)((Dout + Dw2Cfg::BD - 1) / Dw2Cfg::BD);
+  p.status = d->status;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set.load() & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(dw2_hprologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Dw2Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dW2 smem)");
+    attr_set.fetch_or(1ull << dev);
+  }
+  const int tiles = p.tiles_j * p.tiles_d;
+  const int grid = tiles < d->sms ? tiles : d->sms;
+  dw2_hprologue_kernel<<<grid, Dw2Cfg::NUM_THREADS, Dw2Cfg::SMEM_BYTES, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "dW2 launch");
 }
 
 int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int64_t H, int64_t Dout, int dtype,
@@ -427,7 +440,7 @@ int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int6
   p.tiles_m = (int)((M + 127) / 128);
   p.tiles_n = (int)((H + 255) / 256);
   p.group_m = 16;
-  return launch_tc<TcCfg<256, false, true, kEpiDswiglu, false, false>>(p, *d, st);
+  return launch_tc<TcCfg<256, false, true, kEpiDswiglu, false>>(p, *d, st);
 }
 
 int op_fwd_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout, cudaStream_t st) {

@@ -200,7 +200,10 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_fmt, i
 // ------------------------------------------------------------- numerics
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// sigmoid(x) = 1 / (1 + e^-x) with the hardware exp2 and reciprocal
+// approximations (__expf, __fdividef): a few fp32 ulps, far below the bf16
+// rounding applied to every result that uses it. Saturates to 0 / 1.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

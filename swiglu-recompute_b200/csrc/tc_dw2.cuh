@@ -1,0 +1,262 @@
+// dW2 = grad_y^T . h with h = left * silu(gate) recomputed from preact in the
+// GEMM's operand prologue (swiglu_recompute.py:71-73;
+// fused_forward_packed.py:310-311), on tcgen05.
+//
+// The kernel computes dW2^T tiles, D[hidden j, out d] = sum_t h[t, j] grad_y[t, d]:
+//   A = h^T  [128 hidden units x K tokens]  built in shared memory by the
+//            transform warps from the TMA-loaded left and gate tiles
+//   B = grad_y [K tokens x 512 outputs]     TMA-loaded, two N=256 MMAs
+//   D        128 TMEM lanes x 512 columns (the whole TMEM, one accumulator)
+// so each h element is recomputed Dout/512 times (7 at Dout=3584) instead of
+// once per 128-row output tile, and the element-wise work stays well below
+// the tensor core's consumption rate. The epilogue writes D transposed into
+// dW2 [Dout, H]: lane j holds hidden unit j, so each warp store covers 32
+// consecutive hidden units of one output row (64 contiguous bytes).
+//
+// Warps: 0 TMA producer, 1 TMEM alloc + MMA issuer, 2..5 epilogue,
+// 6..9 h prologue. Every wait is bounded (see ptx.cuh).
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace swiglu {
+
+struct Dw2Params {
+  CUtensorMap tm_pre;  // preact [M, 2H], box {64 cols, BK tokens}
+  CUtensorMap tm_gy;   // grad_y [M, Dout], box {64 outs, BK tokens}
+  __nv_bfloat16* dw2;  // [Dout, H]
+  int M, H, Dout;
+  int layout;
+  int tiles_j, tiles_d;  // hidden blocks of 128, output blocks of 512
+  uint32_t* status;
+};
+
+struct Dw2Cfg {
+  static constexpr int BJ = 128;  // hidden units per tile (UMMA M)
+  static constexpr int BD = 512;  // outputs per tile (two UMMA N=256)
+  static constexpr int BK = 32;   // tokens per stage
+  static constexpr int BOX_BYTES = 64 * BK * 2;     // one {64, BK} bf16 box
+  static constexpr int A_BYTES = BJ * BK * 2;       // h^T (left, transformed in place)
+  static constexpr int G_BYTES = BJ * BK * 2;       // gate
+  static constexpr int B_BYTES = BD * BK * 2;       // grad_y
+  static constexpr int STAGE_BYTES = A_BYTES + G_BYTES + B_BYTES;
+  static constexpr int STAGES = 4;
+  static constexpr int NUM_XFORM_WARPS = 4;
+  static constexpr int NUM_THREADS = 32 * (2 + 4 + NUM_XFORM_WARPS);
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (3 * STAGES + 3) + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(Dw2Cfg::NUM_THREADS, 1) dw2_hprologue_kernel(const __grid_constant__ Dw2Params p) {
+  using C = Dw2Cfg;
+  constexpr int STAGES = C::STAGES, BK = C::BK;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;                // TMA -> transform
+  uint64_t* ready = bars + STAGES;      // transform -> MMA
+  uint64_t* empty = bars + 2 * STAGES;  // MMA -> TMA
+  uint64_t* tmem_full = bars + 3 * STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* mma_done = tmem_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], C::NUM_XFORM_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 4);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.tiles_j * p.tiles_d;
+  const int num_kb = (p.M + BK - 1) / BK;
+  uint32_t* status = p.status;
+
+  // Tiles are visited output-block fastest: CTAs running together share the
+  // same hidden block's left/gate rows and stream the same grad_y rows.
+  auto tile_jd = [&](int tile, int& tj, int& td) {
+    tj = tile / p.tiles_d;
+    td = tile - tj * p.tiles_d;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_pre);
+      tma_prefetch_desc(&p.tm_gy);
+      uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tj, td;
+        tile_jd(tile, tj, td);
+        const int j0 = tj * C::BJ;
+        const int lc = left_col(j0, p.H, p.layout);
+        const int gc = gate_col(j0, p.H, p.layout);
+        const int d0 = td * C::BD;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sg = sa + C::A_BYTES;
+          uint8_t* sb = sg + C::G_BYTES;
+          const int t0 = kb * BK;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &p.tm_pre, &full[stage], lc, t0);
+          tma_load_2d(sa + C::BOX_BYTES, &p.tm_pre, &full[stage], lc + 64, t0);
+          tma_load_2d(sg, &p.tm_pre, &full[stage], gc, t0);
+          tma_load_2d(sg + C::BOX_BYTES, &p.tm_pre, &full[stage], gc + 64, t0);
+#pragma unroll
+          for (int i = 0; i < C::BD / 64; ++i) tma_load_2d(sb + i * C::BOX_BYTES, &p.tm_gy, &full[stage], d0 + 64 * i, t0);
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        if (filled & (1u << s)) {
+          volatile int never = 0;
+          mbar_wait(&full[s], (fill_parity >> s) & 1u, &never, status, kErrTimeoutTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(128, 256, 1, 1, 1, 1);  // both operands MN-major
+      uint32_t stage = 0, phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(tmem_empty, acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+        tc_fence_after_sync();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ready[stage], phase, abort_flag, status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES + C::G_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = make_smem_desc_sw128(sa + k * 2048, C::BOX_BYTES, 1024);
+            const uint64_t b0 = make_smem_desc_sw128(sb + k * 2048, C::BOX_BYTES, 1024);
+            const uint64_t b1 = make_smem_desc_sw128(sb + 4 * C::BOX_BYTES + k * 2048, C::BOX_BYTES, 1024);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            umma_f16_ss(tmem_base, adesc, b0, idesc, acc);
+            umma_f16_ss(tmem_base + 256, adesc, b1, idesc, acc);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tmem_full);
+        acc_phase ^= 1;
+      }
+      umma_commit(mma_done);
+      volatile int never = 0;
+      mbar_wait(mma_done, 0, &never, status, kErrTimeoutTeardown);
+    }
+  } else if (warp < 6) {
+    // Epilogue: lane = hidden unit, 32 consecutive outputs per TMEM load.
+    const uint32_t q = warp & 3u;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tj, td;
+      tile_jd(tile, tj, td);
+      if (!mbar_wait(tmem_full, acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
+      tc_fence_after_sync();
+      const int j = tj * C::BJ + static_cast<int>(q * 32 + lane);
+      const bool j_ok = j < p.H;
+      const int d0 = td * C::BD;
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16);
+#pragma unroll 1
+      for (int c = 0; c < C::BD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int dc = d0 + c * 32;
+        if (j_ok) {
+          __nv_bfloat16* col = p.dw2 + static_cast<long long>(dc) * p.H + j;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (dc + i < p.Dout) col[static_cast<long long>(i) * p.H] = __float2bfloat16_rn(__uint_as_float(r[i]));
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_empty);
+      acc_phase ^= 1;
+    }
+  } else {
+    // h prologue: A (left) and G (gate) were loaded with the same boxes, so
+    // h = left * silu(gate) is formed at matching swizzled positions.
+    const uint32_t xt = threadIdx.x - 32 * 6;
+    constexpr int kChunks = C::A_BYTES / 16;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
+          ok = false;
+          break;
+        }
+        uint4* sa = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
+        const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * C::STAGE_BYTES + C::A_BYTES);
+#pragma unroll
+        for (int i = static_cast<int>(xt); i < kChunks; i += 32 * C::NUM_XFORM_WARPS) {
+          const uint4 lu = sa[i];
+          const uint4 gu = sg[i];
+          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+          uint32_t hw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 l2 = unpack_bf16x2(lw[e]);
+            const float2 g2 = unpack_bf16x2(gw[e]);
+            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
+          }
+          sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace swiglu

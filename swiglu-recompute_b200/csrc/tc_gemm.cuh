@@ -14,7 +14,6 @@
 //   warp 0      TMA producer (one elected lane)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
 //   warps 2..5  epilogue: TMEM -> registers -> epilogue math -> global
-//   warps 6..9  (kTransform only) operand prologue: B <- left * silu(gate)
 //
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the
 // epilogue of tile i overlaps the main loop of tile i+1.
@@ -28,8 +27,7 @@
 //   kEpiDswiglu  backward grad_h GEMM: D = grad_h; reads preact, writes
 //                grad_left / grad_gate over it in place
 //                (swiglu_recompute.py:33-49, fused_forward_packed.py:222-259)
-// kTransform: the B operand is h recomputed from preact in shared memory
-//                (swiglu_recompute.py:71-73 / fused_forward_packed.py:310-311).
+// The dW2 GEMM with the h prologue is a separate kernel (tc_dw2.cuh).
 #pragma once
 
 #include "ptx.cuh"
@@ -53,11 +51,11 @@ __host__ __device__ __forceinline__ int gate_col(int j, int H, int layout) {
 
 struct TcParams {
   CUtensorMap tmA;  // A operand (box: K-major {64,128} / MN-major {64,64})
-  CUtensorMap tmB;  // B operand, or preact when kTransform (box: K-major {64,BN/2} / MN-major {64,64})
+  CUtensorMap tmB;  // B operand (box: K-major {64,BN/2} / MN-major {64,64})
   void* out0;       // store: D; swiglu: preact; dswiglu: preact (in/out)
   void* out1;       // swiglu: h (may be null)
   long long ld0, ld1;
-  int M, N, K;      // N: output columns (swiglu/dswiglu/transform: hidden units)
+  int M, N, K;      // N: output columns (swiglu/dswiglu: hidden units)
   int H;            // hidden width (column maps)
   int layout;       // kLayoutStd / kLayoutPacked
   int tiles_m, tiles_n, group_m;
@@ -69,7 +67,7 @@ struct TcParams {
 
 constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
 
-template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool TRANSFORM_, bool OUT_F32_>
+template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
 struct TcCfg {
   static constexpr int BM = 128;
   static constexpr int BN = BN_;
@@ -77,25 +75,21 @@ struct TcCfg {
   static constexpr bool A_MN = A_MN_;
   static constexpr bool B_MN = B_MN_;
   static constexpr int EPI = EPI_;
-  static constexpr bool TRANSFORM = TRANSFORM_;
   static constexpr bool OUT_F32 = OUT_F32_;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int G_BYTES = TRANSFORM ? B_BYTES : 0;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + G_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES;
   static constexpr int SMEM_BUDGET = 200 * 1024;
   static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static constexpr int NUM_EPI_WARPS = 4;
-  static constexpr int NUM_XFORM_WARPS = TRANSFORM ? 4 : 0;
-  static constexpr int NUM_THREADS = 32 * (2 + NUM_EPI_WARPS + NUM_XFORM_WARPS);
-  static constexpr int BAR_BYTES = 8 * (4 * STAGES + 5) + 16;
+  static constexpr int NUM_THREADS = 32 * (2 + NUM_EPI_WARPS);
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
-  static_assert(!(TRANSFORM && !B_MN), "the h prologue reads preact rows (MN-major B)");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& pm, int& pn) {
@@ -145,10 +139,9 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
   // 128-byte swizzled TMA boxes and UMMA atoms need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
-  uint64_t* full = bars;                    // TMA -> (transform | MMA)
+  uint64_t* full = bars;                    // TMA -> MMA
   uint64_t* empty = bars + STAGES;          // MMA -> TMA
-  uint64_t* ready = bars + 2 * STAGES;      // transform -> MMA
-  uint64_t* tmem_full = bars + 3 * STAGES;  // MMA -> epilogue (2)
+  uint64_t* tmem_full = bars + 2 * STAGES;  // MMA -> epilogue (2)
   uint64_t* tmem_empty = tmem_full + 2;     // epilogue -> MMA (2)
   uint64_t* mma_done = tmem_empty + 2;      // MMA teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -161,7 +154,6 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&ready[s], Cfg::NUM_XFORM_WARPS > 0 ? Cfg::NUM_XFORM_WARPS : 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
@@ -196,19 +188,12 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
         int pm, pn;
         tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
         const int m0 = pm * BM;
-        // Origins of the two B halves (BN/2 columns each) and, for the h
-        // prologue, of the two gate halves.
-        int b0, b1, g0 = 0, g1 = 0;
+        // Origins of the two B halves (BN/2 columns each).
+        int b0, b1;
         if constexpr (Cfg::EPI == kEpiSwiglu) {
           const int j0 = pn * (BN / 2);
           b0 = left_col(j0, p.H, p.layout);
           b1 = gate_col(j0, p.H, p.layout);
-        } else if constexpr (Cfg::TRANSFORM) {
-          const int j0 = pn * BN;
-          b0 = left_col(j0, p.H, p.layout);
-          b1 = b0 + BN / 2;
-          g0 = gate_col(j0, p.H, p.layout);
-          g1 = g0 + BN / 2;
         } else {
           b0 = pn * BN;
           b1 = b0 + BN / 2;
@@ -220,7 +205,6 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
-          uint8_t* sg = sb + Cfg::B_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::TX_BYTES);
           const int k0 = kb * BK;
           if constexpr (Cfg::A_MN) {
@@ -237,13 +221,6 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
 #pragma unroll
             for (int i = 0; i < BN / 128; ++i) {
               tma_load_2d(sb + (BN / 128 + i) * 8192, &p.tmB, &full[stage], b1 + 64 * i, k0);
-            }
-            if constexpr (Cfg::TRANSFORM) {
-#pragma unroll
-              for (int i = 0; i < BN / 128; ++i) tma_load_2d(sg + i * 8192, &p.tmB, &full[stage], g0 + 64 * i, k0);
-#pragma unroll
-              for (int i = 0; i < BN / 128; ++i)
-                tma_load_2d(sg + (BN / 128 + i) * 8192, &p.tmB, &full[stage], g1 + 64 * i, k0);
             }
           } else {
             tma_load_2d(sb, &p.tmB, &full[stage], k0, b0);
@@ -276,8 +253,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          uint64_t* wait_bar = Cfg::TRANSFORM ? &ready[stage] : &full[stage];
-          if (!mbar_wait(wait_bar, phase, abort_flag, status, kErrTimeoutMma)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -363,7 +339,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
               l = bf16_round(l);
               g = bf16_round(g);
             }
-            hf[i] = l * (g * sigmoidf_(g));
+            hf[i] = l * (g * sigmoid_fast(g));
           }
           if (row_ok) {
             store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
@@ -402,7 +378,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
                 const int i = 8 * v8 + 2 * e + u;
                 // grad_h is a bf16 tensor in the reference before the pointwise step.
                 const float dh = bf16_round(__uint_as_float(r[i]));
-                const float sg = sigmoidf_(gs[u]);
+                const float sg = sigmoid_fast(gs[u]);
                 const float silu = gs[u] * sg;
                 const float dsilu = sg + silu * (1.0f - sg);
                 gl[i] = dh * silu;
@@ -421,47 +397,6 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
-      }
-    }
-  } else if constexpr (Cfg::TRANSFORM) {
-    // -------------------------------------------- operand prologue: h tiles
-    // B (left) and G (gate) boxes share one layout, so h is formed element by
-    // element at the same swizzled positions without decoding the swizzle.
-    const uint32_t xt = threadIdx.x - 32 * (2 + Cfg::NUM_EPI_WARPS);
-    constexpr int kChunks = Cfg::B_BYTES / 16;
-    uint32_t stage = 0, phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
-          ok = false;
-          break;
-        }
-        uint4* sb = reinterpret_cast<uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES);
-        const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES +
-                                                         Cfg::B_BYTES);
-#pragma unroll 4
-        for (int i = static_cast<int>(xt); i < kChunks; i += 32 * Cfg::NUM_XFORM_WARPS) {
-          const uint4 lu = sb[i];
-          const uint4 gu = sg[i];
-          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
-          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-          uint32_t hw[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 l2 = unpack_bf16x2(lw[e]);
-            const float2 g2 = unpack_bf16x2(gw[e]);
-            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoidf_(g2.x)), l2.y * (g2.y * sigmoidf_(g2.y)));
-          }
-          sb[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
       }
     }
   }
