@@ -203,6 +203,46 @@ def kernel_flops(M, D, H, Dout):
             "dw1": g1, "dx": g1}
 
 
+def run_kernel_only(args):
+    """Launch one kernel of the step `args.iters` times at config-2 shapes
+    (the case the committed ncu summaries under profiles/ are taken on)."""
+    from swiglu_b200 import ops
+    from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, D, H, Dout = CFG["M"], CFG["D"], CFG["H"], CFG["Dout"]
+    x, w1, w2, gy = (t.to(dev) for t in _inputs(dev))
+    preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+    k = args.kernel
+    calls = {
+        "gemm1": lambda: ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True),
+        "y": lambda: ops.matmul(h, w2, a_t=False, b_t=True),
+        "dw2": lambda: ops.bwd_dw2(gy, preact, layout=LAYOUT_STD),
+        # in place on a scratch copy so repeated launches see the same input
+        "gradh": lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD),
+        "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False),
+        "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False),
+    }
+    pre2 = torch.empty_like(preact) if k == "gradh" else None
+    fl = kernel_flops(M, D, H, Dout)[{"gemm1": "gemm1_swiglu", "y": "gemm2_y", "dw2": "dw2_hprologue",
+                                      "gradh": "gradh_dswiglu_inplace", "dw1": "dw1", "dx": "dx"}[k]]
+    times = []
+    for _ in range(args.iters):
+        if pre2 is not None:
+            pre2.copy_(preact)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        calls[k]()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    assert ops.device_status(0) == 0
+    best = min(times)
+    print(json.dumps({"kernel": k, "ms": round(best, 4), "tflops": round(fl / best / 1e9, 1),
+                      "times_ms": [round(t, 4) for t in times]}), flush=True)
+
+
 def run_ours_single(args):
     import swiglu_recompute as SR
     from swiglu_b200 import ops
@@ -310,12 +350,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "gradh", "dw1", "dx"],
+                    help="launch only this kernel (profiling case)")
+    ap.add_argument("--iters", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
 
+    if args.kernel:
+        run_kernel_only(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return

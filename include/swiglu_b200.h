@@ -65,6 +65,14 @@ const char* swiglu_b200_last_error_message(void);
  * a bit mask of kernel pipeline timeouts. Synchronises the device. 0 = healthy. */
 int swiglu_b200_device_status(uint32_t* bits, int clear);
 
+/* Selects the tcgen05 GEMM kernel family for subsequent calls (process-wide):
+ * 0 = by problem size (default), 1 = single-SM kernel (128-row tiles),
+ * 2 = 2-SM kernel (cta_group::2, 256-row tiles on a CTA pair).
+ * Results are identical up to f32 summation order; this exists for testing
+ * and tuning. No reference counterpart (the reference's Triton kernels pick
+ * their tiling at compile time, fused_forward.py:55-65). */
+int swiglu_b200_set_gemm_path(int mode);
+
 /* One launch: preact [M, 2H] = x [M, K] . W1^T and h [M, H] = left * silu(gate).
  * h may be NULL (preact only).
  *   w_form = T, layout = STD:       fused_matmul_swiglu_save_preact   fused_forward.py:188-256

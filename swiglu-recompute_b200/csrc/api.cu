@@ -13,6 +13,7 @@
 
 #include "simt_kernels.cuh"
 #include "tc_dw2.cuh"
+#include "tc_gemm2.cuh"
 
 namespace swiglu {
 
@@ -195,6 +196,65 @@ int launch_tc(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
   return SWIGLU_OK;
 }
 
+// GEMM kernel choice: 0 = by size, 1 = single-SM kernel, 2 = 2-SM kernel.
+std::atomic<int> g_gemm_path{0};
+
+template <class Cfg>
+int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_set{0};
+  static int max_clusters[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = tc_gemm2_kernel<Cfg>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::NUM_THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!(attr_set.load() & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem, 2-SM)");
+    cfg.gridDim = dim3(2 * (d.sms / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+    if (n < 1) return fail(SWIGLU_ERR_CUDA, "no CTA pair fits on device %d", dev);
+    max_clusters[dev] = n;
+    attr_set.fetch_or(1ull << dev);
+  }
+  p.mn_lbo = kMnLbo;
+  p.mn_sbo = kMnSbo;
+  p.status = d.status;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int clusters = tiles < max_clusters[dev] ? tiles : max_clusters[dev];
+  cfg.gridDim = dim3(2 * clusters);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return cuda_fail(e, "2-SM tcgen05 GEMM launch");
+  return SWIGLU_OK;
+}
+
+// Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
+// the 2-SM (256-row tiles) kernel. p.tiles_n must be set; tiles_m is set here.
+template <bool A_MN, bool B_MN, int EPI, bool F32>
+int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+  const int tiles2 = ((p.M + 255) / 256) * p.tiles_n;
+  int mode = g_gemm_path.load(std::memory_order_relaxed);
+  // By size: pairs pay off once there is at least one full wave of them.
+  if (mode == 0) mode = tiles2 >= d.sms / 2 ? 2 : 1;
+  if (mode == 2) {
+    p.tiles_m = (p.M + 255) / 256;
+    return launch_tc2<Tc2Cfg<A_MN, B_MN, EPI, F32>>(p, d, st);
+  }
+  p.tiles_m = (p.M + 127) / 128;
+  return launch_tc<TcCfg<256, A_MN, B_MN, EPI, F32>>(p, d, st);
+}
+
 template <bool A_MN, bool B_MN, int EPI, bool TRANSFORM>
 int launch_simt(const SimtParams& p, int ntile_cols, cudaStream_t st) {
   dim3 grid(ntile_cols, (p.M + 63) / 64);
@@ -280,14 +340,13 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   p.ld0 = 2 * H;
   p.ld1 = H;
   p.M = (int)M, p.N = (int)H, p.K = (int)K, p.H = (int)H, p.layout = layout;
-  p.tiles_m = (int)((M + 127) / 128);
   p.tiles_n = (int)((H + 127) / 128);
   p.group_m = group_m;
   p.flags = rounded ? kFlagHFromRounded : 0;
   if (reinterpret_cast<uintptr_t>(preact) % 16 || (h && reinterpret_cast<uintptr_t>(h) % 16))
     return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
-  return w_form == SWIGLU_W1_ROWS ? launch_tc<TcCfg<256, false, false, kEpiSwiglu, false>>(p, *d, st)
-                                  : launch_tc<TcCfg<256, false, true, kEpiSwiglu, false>>(p, *d, st);
+  return w_form == SWIGLU_W1_ROWS ? run_gemm<false, false, kEpiSwiglu, false>(p, *d, st)
+                                  : run_gemm<false, true, kEpiSwiglu, false>(p, *d, st);
 }
 
 int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout, int b_layout,
@@ -342,11 +401,10 @@ int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64
   p.out0 = c;
   p.ld0 = N;
   p.M = (int)M, p.N = (int)N, p.K = (int)K, p.H = 0, p.layout = 0;
-  p.tiles_m = (int)((M + 127) / 128);
   p.tiles_n = (int)((N + 255) / 256);
   p.group_m = group_m;
   const bool f32 = out_dtype == SWIGLU_F32;
-#define SWIGLU_MM(AM, BM_, F) launch_tc<TcCfg<256, AM, BM_, kEpiStore, F>>(p, *d, st)
+#define SWIGLU_MM(AM, BM_, F) run_gemm<AM, BM_, kEpiStore, F>(p, *d, st)
   if (f32) {
     if (a_mn) return b_mn ? SWIGLU_MM(true, true, true) : SWIGLU_MM(true, false, true);
     return b_mn ? SWIGLU_MM(false, true, true) : SWIGLU_MM(false, false, true);
@@ -437,10 +495,9 @@ int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int6
   p.out0 = preact;
   p.ld0 = 2 * H;
   p.M = (int)M, p.N = (int)H, p.K = (int)Dout, p.H = (int)H, p.layout = layout;
-  p.tiles_m = (int)((M + 127) / 128);
   p.tiles_n = (int)((H + 255) / 256);
   p.group_m = 16;
-  return launch_tc<TcCfg<256, false, true, kEpiDswiglu, false>>(p, *d, st);
+  return run_gemm<false, true, kEpiDswiglu, false>(p, *d, st);
 }
 
 int op_fwd_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout, cudaStream_t st) {
@@ -546,6 +603,12 @@ int swiglu_b200_device_status(uint32_t* bits, int clear) {
   }
   *bits = v;
   return v ? fail(SWIGLU_ERR_DEVICE_TIMEOUT, "kernel pipeline wait timed out (bits 0x%x)", v) : SWIGLU_OK;
+}
+
+int swiglu_b200_set_gemm_path(int mode) {
+  if (mode < 0 || mode > 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "gemm path must be 0, 1 or 2");
+  g_gemm_path.store(mode);
+  return SWIGLU_OK;
 }
 
 int swiglu_b200_fused_matmul_swiglu_save_preact(const void* x, const void* w, void* preact, void* h, int64_t M,

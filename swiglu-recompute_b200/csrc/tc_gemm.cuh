@@ -131,6 +131,104 @@ __device__ __forceinline__ void store_row32(void* row_ptr, int c0, int ncols, co
   }
 }
 
+// Epilogue of one output tile for the 32 rows of one warp: row `row` of the
+// output (this thread's TMEM lane) and its TMEM address `t_row` (lane base +
+// accumulator column base). Tile (pm, pn) of BN accumulator columns.
+template <int BN, int EPI, bool OUT_F32>
+__device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn, int row, uint32_t t_row) {
+  const bool row_ok = row < p.M;
+  if constexpr (EPI == kEpiStore) {
+    const int n0 = pn * BN;
+    char* out_row = reinterpret_cast<char*>(p.out0) +
+                    (static_cast<long long>(row) * p.ld0) * (OUT_F32 ? 4 : 2);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c * 32, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (row_ok) store_row32<OUT_F32>(out_row, n0 + c * 32, p.N, v);
+    }
+  } else if constexpr (EPI == kEpiSwiglu) {
+    const int j0 = pn * (BN / 2);
+    __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+    __nv_bfloat16* h_row =
+        p.out1 ? reinterpret_cast<__nv_bfloat16*>(p.out1) + static_cast<long long>(row) * p.ld1 : nullptr;
+    const bool rounded = (p.flags & kFlagHFromRounded) != 0;
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t rl[32], rg[32];
+      tmem_ld_32x32b_x32(t_row + c * 32, rl);
+      tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
+      tmem_ld_wait();
+      const int j = j0 + c * 32;  // first hidden unit of this chunk (multiple of 32)
+      float lf[32], gf[32], hf[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float l = __uint_as_float(rl[i]);
+        float g = __uint_as_float(rg[i]);
+        lf[i] = l;
+        gf[i] = g;
+        if (rounded) {
+          l = bf16_round(l);
+          g = bf16_round(g);
+        }
+        hf[i] = l * (g * sigmoid_fast(g));
+      }
+      if (row_ok) {
+        store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
+        store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
+        if (h_row) store_row32<false>(h_row, j, p.N, hf);
+      }
+    }
+  } else {  // kEpiDswiglu
+    const int j0 = pn * BN;
+    __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c * 32, r);
+      tmem_ld_wait();
+      const int j = j0 + c * 32;
+      if (row_ok) {
+        const int lc = left_col(j, p.H, p.layout);
+        const int gc = gate_col(j, p.H, p.layout);
+        float gl[32], gg[32];
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          if (j + 8 * v8 + 8 > p.N) continue;
+          const uint4 lu = *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8);
+          const uint4 gu = *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8);
+          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 l2 = unpack_bf16x2(lw[e]);
+            const float2 g2 = unpack_bf16x2(gw[e]);
+            const float ls[2] = {l2.x, l2.y};
+            const float gs[2] = {g2.x, g2.y};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int i = 8 * v8 + 2 * e + u;
+              // grad_h is a bf16 tensor in the reference before the pointwise step.
+              const float dh = bf16_round(__uint_as_float(r[i]));
+              const float sg = sigmoid_fast(gs[u]);
+              const float silu = gs[u] * sg;
+              const float dsilu = sg + silu * (1.0f - sg);
+              gl[i] = dh * silu;
+              gg[i] = dh * ls[u] * dsilu;
+            }
+          }
+        }
+        store_row32<false>(pre_row, lc, lc + (p.N - j), gl);
+        store_row32<false>(pre_row, gc, gc + (p.N - j), gg);
+      }
+    }
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
@@ -298,99 +396,9 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
       if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
       tc_fence_after_sync();
       const int row = pm * BM + static_cast<int>(q * 32 + lane);
-      const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
 
-      if constexpr (Cfg::EPI == kEpiStore) {
-        const int n0 = pn * BN;
-        char* out_row = reinterpret_cast<char*>(p.out0) +
-                        (static_cast<long long>(row) * p.ld0) * (Cfg::OUT_F32 ? 4 : 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tmem_ld_wait();
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          if (row_ok) store_row32<Cfg::OUT_F32>(out_row, n0 + c * 32, p.N, v);
-        }
-      } else if constexpr (Cfg::EPI == kEpiSwiglu) {
-        const int j0 = pn * (BN / 2);
-        __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
-        __nv_bfloat16* h_row =
-            p.out1 ? reinterpret_cast<__nv_bfloat16*>(p.out1) + static_cast<long long>(row) * p.ld1 : nullptr;
-        const bool rounded = (p.flags & kFlagHFromRounded) != 0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t rl[32], rg[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, rl);
-          tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
-          tmem_ld_wait();
-          const int j = j0 + c * 32;  // first hidden unit of this chunk (multiple of 32)
-          float lf[32], gf[32], hf[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float l = __uint_as_float(rl[i]);
-            float g = __uint_as_float(rg[i]);
-            lf[i] = l;
-            gf[i] = g;
-            if (rounded) {
-              l = bf16_round(l);
-              g = bf16_round(g);
-            }
-            hf[i] = l * (g * sigmoid_fast(g));
-          }
-          if (row_ok) {
-            store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
-            store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
-            if (h_row) store_row32<false>(h_row, j, p.N, hf);
-          }
-        }
-      } else {  // kEpiDswiglu
-        const int j0 = pn * BN;
-        __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, r);
-          tmem_ld_wait();
-          const int j = j0 + c * 32;
-          if (row_ok) {
-          const int lc = left_col(j, p.H, p.layout);
-          const int gc = gate_col(j, p.H, p.layout);
-          float gl[32], gg[32];
-#pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            if (j + 8 * v8 + 8 > p.N) continue;
-            const uint4 lu = *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8);
-            const uint4 gu = *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8);
-            const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
-            const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 l2 = unpack_bf16x2(lw[e]);
-              const float2 g2 = unpack_bf16x2(gw[e]);
-              const float ls[2] = {l2.x, l2.y};
-              const float gs[2] = {g2.x, g2.y};
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int i = 8 * v8 + 2 * e + u;
-                // grad_h is a bf16 tensor in the reference before the pointwise step.
-                const float dh = bf16_round(__uint_as_float(r[i]));
-                const float sg = sigmoid_fast(gs[u]);
-                const float silu = gs[u] * sg;
-                const float dsilu = sg + silu * (1.0f - sg);
-                gl[i] = dh * silu;
-                gg[i] = dh * ls[u] * dsilu;
-              }
-            }
-          }
-          store_row32<false>(pre_row, lc, lc + (p.N - j), gl);
-          store_row32<false>(pre_row, gc, gc + (p.N - j), gg);
-          }
-        }
-      }
+      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[acc]);

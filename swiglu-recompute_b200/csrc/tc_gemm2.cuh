@@ -1,0 +1,224 @@
+// 2-SM (cta_group::2) variant of the persistent warp-specialized GEMM.
+//
+// A cluster of two CTAs on neighbouring SMs computes one 256 x 256 output
+// tile with M=256 tcgen05.mma instructions issued by rank 0. Each CTA stages
+// only its half of the operands (A rows [128r, 128r+128) and B columns
+// [128r, 128r+128)) and its TMEM receives its 128 rows of D, so per SM the
+// shared-memory footprint per MMA-clock and the L2 operand traffic are half
+// those of the single-SM kernel (tc_gemm.cuh): 6 pipeline stages fit.
+//
+// Protocol (all waits bounded):
+//   both CTAs' producers wait on their own `empty[s]` and TMA-load their halves
+//     with completion counted on rank 0's `full[s]` (rank 0 posts the
+//     expected byte count of both halves);
+//   rank 0's MMA thread waits `full[s]`, issues the pair MMAs and commits to
+//     `empty[s]` of both CTAs, and per tile to `tmem_full[acc]` of both CTAs;
+//   both CTAs' epilogue warps drain their TMEM rows and arrive on rank 0's
+//     `tmem_empty[acc]` (8 arrivals: 4 warps x 2 CTAs).
+// Epilogues are the same as the single-SM kernel's (epilogue_tile).
+//
+// No TMA multicast is used: each CTA loads its own halves.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace swiglu {
+
+template <bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
+struct Tc2Cfg {
+  static constexpr int BM = 256;   // pair tile rows (128 per CTA)
+  static constexpr int BMH = 128;  // rows per CTA
+  static constexpr int BN = 256;   // tile columns (128 of B per CTA)
+  static constexpr int BK = 64;
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  static constexpr int EPI = EPI_;
+  static constexpr bool OUT_F32 = OUT_F32_;
+  static constexpr int A_BYTES = BMH * BK * 2;      // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int NUM_THREADS = 192;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5) + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __grid_constant__ TcParams p) {
+  constexpr int BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;                    // TMA (both CTAs) -> MMA; used in rank 0
+  uint64_t* empty = bars + STAGES;          // MMA -> TMA, in each CTA
+  uint64_t* tmem_full = bars + 2 * STAGES;  // MMA -> epilogue, in each CTA (2)
+  uint64_t* tmem_empty = tmem_full + 2;     // epilogues -> MMA; used in rank 0 (2)
+  uint64_t* mma_done = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // Both CTAs' barriers exist and TMEM is allocated before any cross-CTA use.
+  tc_fence_before_sync();
+  cluster_sync_all();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int first_tile = static_cast<int>(cluster_id_x());
+  const int tile_step = static_cast<int>(num_clusters_x());
+  uint32_t* status = p.status;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tmA);
+      tma_prefetch_desc(&p.tmB);
+      uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
+      bool ok = true;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+        int pm, pn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+        const int m0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank);
+        int b0;  // first column of this CTA's half of B
+        if constexpr (Cfg::EPI == kEpiSwiglu) {
+          const int j0 = pn * (BN / 2);
+          b0 = leader ? left_col(j0, p.H, p.layout) : gate_col(j0, p.H, p.layout);
+        } else {
+          b0 = pn * BN + (BN / 2) * static_cast<int>(rank);
+        }
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          const uint32_t bar = map_to_rank(&full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (Cfg::A_MN) {
+            tma_load_2d_pair(sa, &p.tmA, bar, m0, k0);
+            tma_load_2d_pair(sa + 64 * BK * 2, &p.tmA, bar, m0 + 64, k0);
+          } else {
+            tma_load_2d_pair(sa, &p.tmA, bar, k0, m0);
+          }
+          if constexpr (Cfg::B_MN) {
+            tma_load_2d_pair(sb, &p.tmB, bar, b0, k0);
+            tma_load_2d_pair(sb + 64 * BK * 2, &p.tmB, bar, b0 + 64, k0);
+          } else {
+            tma_load_2d_pair(sb, &p.tmB, bar, k0, b0);
+          }
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: a stage this CTA filled is finished once the MMA released it.
+      for (int s = 0; s < STAGES; ++s) {
+        if (filled & (1u << s)) {
+          volatile int never = 0;
+          mbar_wait(&empty[s], (fill_parity >> s) & 1u, &never, status, kErrTimeoutTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_f16(256, BN, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
+                                             : make_smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sb + k * 2048, p.mn_lbo, p.mn_sbo)
+                                             : make_smem_desc_sw128(sb + k * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(map_to_rank(&empty[stage], 0));
+          umma_commit_pair(map_to_rank(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(map_to_rank(&tmem_full[acc], 0));
+        umma_commit_pair(map_to_rank(&tmem_full[acc], 1));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair(map_to_rank(mma_done, 0));
+      volatile int never = 0;
+      mbar_wait(mma_done, 0, &never, status, kErrTimeoutTeardown);
+    }
+  } else {
+    const uint32_t q = warp & 3u;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+      int pm, pn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
+      tc_fence_after_sync();
+      const int row = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
+      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row);
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[acc], 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  // Neither CTA releases TMEM (or exits) before the pair is done with it.
+  tc_fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace swiglu

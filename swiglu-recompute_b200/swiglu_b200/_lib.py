@@ -29,6 +29,7 @@ _SIGNATURES = {
     "swiglu_b200_status_string": [_i],
     "swiglu_b200_last_error_message": [],
     "swiglu_b200_device_status": [ctypes.POINTER(ctypes.c_uint32), _i],
+    "swiglu_b200_set_gemm_path": [_i],
     "swiglu_b200_fused_matmul_swiglu_save_preact":
         [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
     "swiglu_b200_matmul": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
@@ -96,6 +97,11 @@ def check(status: int) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args))
+
+
+def set_gemm_path(mode: int) -> None:
+    """0 = by size, 1 = single-SM tcgen05 kernel, 2 = 2-SM (CTA pair) kernel."""
+    call("swiglu_b200_set_gemm_path", int(mode))
 
 
 def device_status(clear: bool = True) -> int:

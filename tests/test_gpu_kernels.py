@@ -9,13 +9,21 @@ import pytest
 import torch
 
 from oracle import swiglu_oracle as O
-from swiglu_b200 import ops
+from swiglu_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
 
 BF16_TOL = 8e-3
 F32_TOL = 1e-5
 DEV = "cuda"
+
+
+@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+def gemm_path(request):
+    """Run the bf16 GEMMs on the single-SM kernel and on the 2-SM (CTA pair) kernel."""
+    _lib.set_gemm_path(request.param)
+    yield request.param
+    _lib.set_gemm_path(0)
 
 
 def _r(*shape, seed=0, scale=1.0, dtype=torch.bfloat16):
@@ -30,8 +38,9 @@ def _tol(dtype):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
-@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 264, 136), (128, 256, 64), (384, 768, 1024)])
-def test_matmul_layouts(dtype, a_t, b_t, M, N, K):
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 264, 136), (128, 256, 64), (384, 768, 1024),
+                                   (1000, 520, 328)])
+def test_matmul_layouts(gemm_path, dtype, a_t, b_t, M, N, K):
     if a_t and M % 8:
         pytest.skip("MN-major A needs M % 8 == 0")
     a = _r(*((K, M) if a_t else (M, K)), seed=1, dtype=dtype)
@@ -42,7 +51,7 @@ def test_matmul_layouts(dtype, a_t, b_t, M, N, K):
     assert O.rel_max(out.cpu(), ref) <= _tol(dtype)
 
 
-def test_matmul_f32_output_of_bf16_gemm():
+def test_matmul_f32_output_of_bf16_gemm(gemm_path):
     a, b = _r(256, 512, seed=3), _r(512, 256, seed=4, scale=512 ** -0.5)
     ref = a.float() @ b.float()
     out = ops.matmul(a.to(DEV), b.to(DEV), a_t=False, b_t=False, out_dtype=torch.float32)
@@ -53,8 +62,8 @@ def test_matmul_f32_output_of_bf16_gemm():
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("form,layout", [(ops.W1_ROWS, O.STD), (ops.W1_T, O.STD), (ops.W1_T, O.PACKED)])
 @pytest.mark.parametrize("rounded", [False, True])
-@pytest.mark.parametrize("M,K,H", [(256, 256, 256), (200, 136, 384), (128, 64, 128)])
-def test_swiglu_forward_epilogue(dtype, form, layout, rounded, M, K, H):
+@pytest.mark.parametrize("M,K,H", [(256, 256, 256), (200, 136, 384), (128, 64, 128), (640, 192, 512)])
+def test_swiglu_forward_epilogue(gemm_path, dtype, form, layout, rounded, M, K, H):
     if layout == O.PACKED and H % 128:
         pytest.skip("packed layout needs H % 128 == 0")
     x = _r(M, K, seed=5, dtype=dtype)
@@ -90,8 +99,8 @@ def test_dw2_with_recomputed_h(dtype, layout, M, H, Dout):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("layout", [O.STD, O.PACKED])
-@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (128, 640, 64)])
-def test_grad_preact_inplace(dtype, layout, M, H, Dout):
+@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (128, 640, 64), (700, 512, 200)])
+def test_grad_preact_inplace(gemm_path, dtype, layout, M, H, Dout):
     lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
     gy = _r(M, Dout, seed=9, dtype=dtype)
     w2 = _r(Dout, H, seed=10, scale=H ** -0.5, dtype=dtype)

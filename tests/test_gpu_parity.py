@@ -148,6 +148,17 @@ def test_leading_batch_dims():
     assert O.rel_max(gx.reshape(-1, D).cpu(), ref["dx"]) <= 7e-3
 
 
+@pytest.mark.parametrize("path", [1, 2])
+def test_forced_gemm_path_full_step(path):
+    from swiglu_b200 import _lib
+    _lib.set_gemm_path(path)
+    try:
+        (x, w1, w2, gy), out = run_variant("recompute", 600, 512, 640, 384, torch.bfloat16, seed=4)
+        check_all(out, x, w1, w2, gy, torch.bfloat16)
+    finally:
+        _lib.set_gemm_path(0)
+
+
 def test_bitwise_deterministic():
     outs = [run_variant("recompute", 384, 512, 640, 256, torch.bfloat16, seed=9)[1] for _ in range(2)]
     for k in ("y", "dx", "dw1", "dw2"):
