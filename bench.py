@@ -166,31 +166,36 @@ def _inputs(dev, dtype=torch.bfloat16):
 
 
 def kernel_breakdown(x, w1, w2, gy, iters):
-    """Per-kernel device time of one fwd+bwd, events between launches on the
-    launching stream. Returns {name: ms per launch}."""
+    """Per-kernel device time of one fwd+bwd: CUDA events between the launches
+    on the launching stream, `iters` steps queued back to back (no host sync
+    in between, so the GPU never idles between kernels). {name: ms/launch}."""
     from swiglu_b200 import ops
     from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
 
     st = torch.cuda.current_stream()
     names = ["gemm1_swiglu", "gemm2_y", "dw2_hprologue", "gradh_dswiglu_inplace", "dw1", "dx"]
-    acc = {n: 0.0 for n in names}
+    evs = []
     for _ in range(iters):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
         ev[0].record(st)
         preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
         ev[1].record(st)
-        ops.matmul(h, w2, a_t=False, b_t=True)
+        y = ops.matmul(h, w2, a_t=False, b_t=True)
         ev[2].record(st)
-        del h
-        ops.bwd_dw2(gy, preact, layout=LAYOUT_STD)
+        del h, y
+        dw2 = ops.bwd_dw2(gy, preact, layout=LAYOUT_STD)
         ev[3].record(st)
         ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD)
         ev[4].record(st)
-        ops.matmul(preact, x, a_t=True, b_t=False)
+        dw1 = ops.matmul(preact, x, a_t=True, b_t=False)
         ev[5].record(st)
-        ops.matmul(preact, w1, a_t=False, b_t=False)
+        dx = ops.matmul(preact, w1, a_t=False, b_t=False)
         ev[6].record(st)
-        torch.cuda.synchronize()
+        del preact, dw2, dw1, dx
+        evs.append(ev)
+    torch.cuda.synchronize()
+    acc = {n: 0.0 for n in names}
+    for ev in evs:
         for i, n in enumerate(names):
             acc[n] += ev[i].elapsed_time(ev[i + 1])
     return {n: v / iters for n, v in acc.items()}
@@ -353,12 +358,17 @@ def main():
     ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2], default=0,
+                    help="tcgen05 kernel family: 0 by size, 1 single-SM, 2 CTA pair")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
 
+    if args.gemm_path:
+        from swiglu_b200 import _lib
+        _lib.set_gemm_path(args.gemm_path)
     if args.kernel:
         run_kernel_only(args)
         return

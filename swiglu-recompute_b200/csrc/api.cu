@@ -174,69 +174,92 @@ int map_mnmajor(CUtensorMap* m, const void* p, int64_t K, int64_t cols, int64_t 
 constexpr uint32_t kMnLbo = 64 * 64 * 2;  // one {64, 64} bf16 box
 constexpr uint32_t kMnSbo = 8 * 128;      // eight 128-byte swizzle rows
 
-template <class Cfg>
-int launch_tc(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_set{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  auto kern = tc_gemm_kernel<Cfg>;
-  if (!(attr_set.load() & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-    attr_set.fetch_or(1ull << dev);
-  }
-  p.mn_lbo = kMnLbo;
-  p.mn_sbo = kMnSbo;
-  p.status = d.status;
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = tiles < d.sms ? tiles : d.sms;
-  kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, st>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
-  return SWIGLU_OK;
-}
-
 // GEMM kernel choice: 0 = by size, 1 = single-SM kernel, 2 = 2-SM kernel.
 std::atomic<int> g_gemm_path{0};
 
-template <class Cfg>
-int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
-  static std::atomic<uint64_t> attr_set{0};
-  static int max_clusters[kMaxDevices] = {};
+// Per-kernel launch state: dynamic shared memory opt-in done (bit per device)
+// and, for cluster kernels, how many CTA pairs fit at once on each device.
+struct KernelState {
+  std::atomic<uint64_t> ready{0};
+  int max_clusters[kMaxDevices] = {};
+};
+
+template <auto Kernel>
+KernelState& kernel_state() {
+  static KernelState s;  // one per kernel function
+  return s;
+}
+
+// Persistent single-CTA launch: one CTA per SM (at most one per tile).
+template <auto kern, class Params>
+int launch_single(const Params& p, int tiles, int threads, int smem, const DeviceInfo& d, cudaStream_t st,
+                  const char* what) {
+  KernelState& ks = kernel_state<kern>();
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = tc_gemm2_kernel<Cfg>;
+  if (!(ks.ready.load() & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    ks.ready.fetch_or(1ull << dev);
+  }
+  const int grid = tiles < d.sms ? tiles : d.sms;
+  kern<<<grid, threads, smem, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, what);
+}
+
+// Persistent CTA-pair launch (clusters of 2): as many pairs as fit at once,
+// at most one per tile.
+template <auto kern, class Params>
+int launch_pair(const Params& p, int tiles, int threads, int smem, const DeviceInfo& d, cudaStream_t st,
+                const char* what) {
+  KernelState& ks = kernel_state<kern>();
+  int dev = 0;
+  cudaGetDevice(&dev);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(Cfg::NUM_THREADS);
-  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!(attr_set.load() & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem, 2-SM)");
+  if (!(ks.ready.load() & (1ull << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, what);
     cfg.gridDim = dim3(2 * (d.sms / 2));
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-    if (n < 1) return fail(SWIGLU_ERR_CUDA, "no CTA pair fits on device %d", dev);
-    max_clusters[dev] = n;
-    attr_set.fetch_or(1ull << dev);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (n < 1) return fail(SWIGLU_ERR_CUDA, "%s: no CTA pair fits on device %d", what, dev);
+    ks.max_clusters[dev] = n;
+    ks.ready.fetch_or(1ull << dev);
   }
+  const int clusters = tiles < ks.max_clusters[dev] ? tiles : ks.max_clusters[dev];
+  cfg.gridDim = dim3(2 * clusters);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, what);
+}
+
+template <class Cfg>
+int launch_tc(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
   p.mn_lbo = kMnLbo;
   p.mn_sbo = kMnSbo;
   p.status = d.status;
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int clusters = tiles < max_clusters[dev] ? tiles : max_clusters[dev];
-  cfg.gridDim = dim3(2 * clusters);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) return cuda_fail(e, "2-SM tcgen05 GEMM launch");
-  return SWIGLU_OK;
+  return launch_single<tc_gemm_kernel<Cfg>>(p, p.tiles_m * p.tiles_n, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, st,
+                       "tcgen05 GEMM launch");
+}
+
+template <class Cfg>
+int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+  p.mn_lbo = kMnLbo;
+  p.mn_sbo = kMnSbo;
+  p.status = d.status;
+  return launch_pair<tc_gemm2_kernel<Cfg>>(p, p.tiles_m * p.tiles_n, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, st,
+                     "2-SM tcgen05 GEMM launch");
 }
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
@@ -441,28 +464,25 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   if (int rc = check_mult8("H", H)) return rc;
   if (int rc = check_mult8("Dout", Dout)) return rc;
   Dw2Params p{};
+  static_assert(Dw2Cfg::BK == Dw2PairCfg::BK, "both dW2 kernels use the same tensor-map boxes");
   if (int rc = make_map(&p.tm_pre, preact, 2 * H, M, 2 * H, Dw2Cfg::BK, "preact")) return rc;
   if (int rc = make_map(&p.tm_gy, gy, Dout, M, Dout, Dw2Cfg::BK, "grad_y")) return rc;
   if (reinterpret_cast<uintptr_t>(dw2) % 16) return fail(SWIGLU_ERR_MISALIGNED, "dW2 must be 16-byte aligned");
   p.dw2 = static_cast<__nv_bfloat16*>(dw2);
   p.M = (int)M, p.H = (int)H, p.Dout = (int)Dout, p.layout = layout;
-  p.tiles_j = (int)((H + Dw2Cfg::BJ - 1) / Dw2Cfg::BJ);
   p.tiles_d = (int)((Dout + Dw2Cfg::BD - 1) / Dw2Cfg::BD);
   p.status = d->status;
-  static std::atomic<uint64_t> attr_set{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_set.load() & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(dw2_hprologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Dw2Cfg::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dW2 smem)");
-    attr_set.fetch_or(1ull << dev);
+  const int pair_tiles = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ) * p.tiles_d;
+  int mode = g_gemm_path.load(std::memory_order_relaxed);
+  if (mode == 0) mode = pair_tiles >= d->sms / 2 ? 2 : 1;
+  if (mode == 2) {
+    p.tiles_j = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ);
+    return launch_pair<dw2_hprologue_pair_kernel>(p, pair_tiles, Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES,
+                       *d, st, "dW2 (CTA pair)");
   }
-  const int tiles = p.tiles_j * p.tiles_d;
-  const int grid = tiles < d->sms ? tiles : d->sms;
-  dw2_hprologue_kernel<<<grid, Dw2Cfg::NUM_THREADS, Dw2Cfg::SMEM_BYTES, st>>>(p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "dW2 launch");
+  p.tiles_j = (int)((H + Dw2Cfg::BJ - 1) / Dw2Cfg::BJ);
+  return launch_single<dw2_hprologue_kernel>(p, p.tiles_j * p.tiles_d, Dw2Cfg::NUM_THREADS, Dw2Cfg::SMEM_BYTES,
+                       *d, st, "dW2");
 }
 
 int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int64_t H, int64_t Dout, int dtype,

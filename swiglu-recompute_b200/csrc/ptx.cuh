@@ -197,9 +197,12 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
   return out;
 }
 
-// Arrive on an mbarrier given by shared::cluster address (possibly the peer's).
+// Arrive on an mbarrier given by shared::cluster address (possibly the
+// peer's), with the instruction's default (.release, .cta) semantics. Callers
+// that wrote shared memory for the tensor core issue fence.proxy.async first;
+// a cluster-scope release here costs a full memory barrier per arrival.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // Whole-cluster execution barrier (all threads of both CTAs).

@@ -14,7 +14,7 @@
 // consecutive hidden units of one output row (64 contiguous bytes).
 //
 // Warps: 0 TMA producer, 1 TMEM alloc + MMA issuer, 2..5 epilogue,
-// 6..9 h prologue. Every wait is bounded (see ptx.cuh).
+// 6.. h prologue. Every wait is bounded (see ptx.cuh).
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -256,6 +256,260 @@ __global__ void __launch_bounds__(Dw2Cfg::NUM_THREADS, 1) dw2_hprologue_kernel(c
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair (cta_group::2) version. A pair tile is 256 hidden units x 512
+// outputs: rank r recomputes h for its hidden units [128r, 128r+128) only and
+// holds 128 of the 256 output columns of each of the two N=256 MMAs, so per
+// SM a 32-token stage is 8 KB left + 8 KB gate + 16 KB grad_y and six stages
+// fit. Barriers:
+//   lg_full[s]  local, left/gate landed (own TMA)        -> own h prologue
+//   b_full[s]   rank 0, both CTAs' grad_y halves landed  -> MMA
+//   ready[s]    rank 0, 8 prologue warps finished h      -> MMA
+//   empty[s]    each CTA, MMA finished with the stage    -> own producer
+//   tmem_full   each CTA; tmem_empty rank 0 (8 epilogue warps)
+// ---------------------------------------------------------------------------
+struct Dw2PairCfg {
+  static constexpr int BJ = 256;   // hidden units per pair tile (UMMA M)
+  static constexpr int BJH = 128;  // per CTA
+  static constexpr int BD = 512;   // outputs per tile (two UMMA N=256)
+  static constexpr int BK = 32;
+  static constexpr int BOX_BYTES = 64 * BK * 2;
+  static constexpr int A_BYTES = BJH * BK * 2;        // left -> h
+  static constexpr int G_BYTES = BJH * BK * 2;        // gate
+  static constexpr int B_BYTES = (BD / 2) * BK * 2;   // this CTA's grad_y columns
+  static constexpr int STAGE_BYTES = A_BYTES + G_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  // Two prologue warps per scheduler: the h recompute is latency- and
+  // issue-bound (ex2 + rcp per element); measured 1.66 -> 1.33 ms at
+  // M=11136 H=14336 Dout=3584 going from 4 to 8 warps.
+  static constexpr int NUM_XFORM_WARPS = 8;
+  static constexpr int NUM_THREADS = 32 * (2 + 4 + NUM_XFORM_WARPS);
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (4 * STAGES + 3) + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
+    dw2_hprologue_pair_kernel(const __grid_constant__ Dw2Params p) {
+  using C = Dw2PairCfg;
+  constexpr int STAGES = C::STAGES, BK = C::BK;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* lg_full = bars;
+  uint64_t* b_full = bars + STAGES;
+  uint64_t* ready = bars + 2 * STAGES;
+  uint64_t* empty = bars + 3 * STAGES;
+  uint64_t* tmem_full = bars + 4 * STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* mma_done = tmem_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&lg_full[s], 1);
+      mbar_init(&b_full[s], 1);
+      mbar_init(&ready[s], 2 * C::NUM_XFORM_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 8);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync_all();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.tiles_j * p.tiles_d;
+  const int num_kb = (p.M + BK - 1) / BK;
+  const int first_tile = static_cast<int>(cluster_id_x());
+  const int tile_step = static_cast<int>(num_clusters_x());
+  uint32_t* status = p.status;
+  auto tile_jd = [&](int tile, int& tj, int& td) {
+    tj = tile / p.tiles_d;
+    td = tile - tj * p.tiles_d;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_pre);
+      tma_prefetch_desc(&p.tm_gy);
+      uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
+      bool ok = true;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+        int tj, td;
+        tile_jd(tile, tj, td);
+        const int j0 = tj * C::BJ + C::BJH * static_cast<int>(rank);
+        const int lc = left_col(j0, p.H, p.layout);
+        const int gc = gate_col(j0, p.H, p.layout);
+        const int d0 = td * C::BD + 128 * static_cast<int>(rank);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sg = sa + C::A_BYTES;
+          uint8_t* sb = sg + C::G_BYTES;
+          const int t0 = kb * BK;
+          mbar_arrive_expect_tx(&lg_full[stage], C::A_BYTES + C::G_BYTES);
+          tma_load_2d(sa, &p.tm_pre, &lg_full[stage], lc, t0);
+          tma_load_2d(sa + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], lc + 64, t0);
+          tma_load_2d(sg, &p.tm_pre, &lg_full[stage], gc, t0);
+          tma_load_2d(sg + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], gc + 64, t0);
+          const uint32_t bbar = map_to_rank(&b_full[stage], 0);
+          if (leader) mbar_arrive_expect_tx(&b_full[stage], 2 * C::B_BYTES);
+          tma_load_2d_pair(sb, &p.tm_gy, bbar, d0, t0);
+          tma_load_2d_pair(sb + C::BOX_BYTES, &p.tm_gy, bbar, d0 + 64, t0);
+          tma_load_2d_pair(sb + 2 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 256, t0);
+          tma_load_2d_pair(sb + 3 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 320, t0);
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        if (filled & (1u << s)) {
+          volatile int never = 0;
+          mbar_wait(&empty[s], (fill_parity >> s) & 1u, &never, status, kErrTimeoutTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_f16(256, 256, 1, 1, 1, 1);
+      uint32_t stage = 0, phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+        if (!mbar_wait(tmem_empty, acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+        tc_fence_after_sync();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&b_full[stage], phase, abort_flag, status, kErrTimeoutMma) ||
+              !mbar_wait(&ready[stage], phase, abort_flag, status, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES + C::G_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = make_smem_desc_sw128(sa + k * 2048, C::BOX_BYTES, 1024);
+            const uint64_t b0 = make_smem_desc_sw128(sb + k * 2048, C::BOX_BYTES, 1024);
+            const uint64_t b1 = make_smem_desc_sw128(sb + 2 * C::BOX_BYTES + k * 2048, C::BOX_BYTES, 1024);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            umma_f16_ss_pair(tmem_base, adesc, b0, idesc, acc);
+            umma_f16_ss_pair(tmem_base + 256, adesc, b1, idesc, acc);
+          }
+          umma_commit_pair(map_to_rank(&empty[stage], 0));
+          umma_commit_pair(map_to_rank(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(map_to_rank(tmem_full, 0));
+        umma_commit_pair(map_to_rank(tmem_full, 1));
+        acc_phase ^= 1;
+      }
+      umma_commit_pair(map_to_rank(mma_done, 0));
+      volatile int never = 0;
+      mbar_wait(mma_done, 0, &never, status, kErrTimeoutTeardown);
+    }
+  } else if (warp < 6) {
+    const uint32_t q = warp & 3u;
+    uint32_t acc_phase = 0;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+      int tj, td;
+      tile_jd(tile, tj, td);
+      if (!mbar_wait(tmem_full, acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
+      tc_fence_after_sync();
+      const int j = tj * C::BJ + C::BJH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const bool j_ok = j < p.H;
+      const int d0 = td * C::BD;
+      const uint32_t t_row = tmem_base + ((q * 32u) << 16);
+#pragma unroll 1
+      for (int c = 0; c < C::BD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int dc = d0 + c * 32;
+        if (j_ok) {
+          __nv_bfloat16* col = p.dw2 + static_cast<long long>(dc) * p.H + j;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (dc + i < p.Dout) col[static_cast<long long>(i) * p.H] = __float2bfloat16_rn(__uint_as_float(r[i]));
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(tmem_empty, 0));
+      acc_phase ^= 1;
+    }
+  } else {
+    const uint32_t xt = threadIdx.x - 32 * 6;
+    constexpr int kChunks = C::A_BYTES / 16;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&lg_full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
+          ok = false;
+          break;
+        }
+        uint4* sa = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
+        const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * C::STAGE_BYTES + C::A_BYTES);
+#pragma unroll
+        for (int i = static_cast<int>(xt); i < kChunks; i += 32 * C::NUM_XFORM_WARPS) {
+          const uint4 lu = sa[i];
+          const uint4 gu = sg[i];
+          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+          uint32_t hw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 l2 = unpack_bf16x2(lw[e]);
+            const float2 g2 = unpack_bf16x2(gw[e]);
+            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
+          }
+          sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(&ready[stage], 0));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 

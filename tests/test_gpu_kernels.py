@@ -85,8 +85,8 @@ def test_swiglu_forward_epilogue(gemm_path, dtype, form, layout, rounded, M, K, 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("layout", [O.STD, O.PACKED])
-@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (1000, 128, 256)])
-def test_dw2_with_recomputed_h(dtype, layout, M, H, Dout):
+@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (1000, 128, 256), (333, 640, 600)])
+def test_dw2_with_recomputed_h(gemm_path, dtype, layout, M, H, Dout):
     lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
     gy = _r(M, Dout, seed=7, dtype=dtype)
     preact = _r(M, 2 * H, seed=8, dtype=dtype)
