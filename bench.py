@@ -56,13 +56,14 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def profile_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+def profile_traffic(kernel):
+    """Per-launch DRAM bytes (read + write) of `kernel` from the committed ncu
+    summary profiles/traffic.md, or None."""
     p = os.path.join(REPO, "profiles", "traffic.md")
     if not os.path.exists(p):
         return None
     with open(p) as f:
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        m = re.search(r"traffic_bytes_per_launch\[" + re.escape(kernel) + r"\]:\s*([0-9.eE+]+)", f.read())
     return float(m.group(1)) if m else None
 
 
@@ -248,6 +249,121 @@ def run_kernel_only(args):
                       "times_ms": [round(t, 4) for t in times]}), flush=True)
 
 
+REFERENCE_STACK_PEAK_MIB = {1: 2275, 2: 2961, 4: 4334, 8: 7078, 16: 12567}   # results_b200.md:38-42
+
+
+def stacked_depth(n_blocks, dev, reps=3, iters=3):
+    """Peak allocated-memory delta (MiB) and ms per fwd+bwd of `n_blocks`
+    stacked config-2 blocks, measured as the reference's stacked-depth
+    benchmark does (bench_stacked_blocks.py:55-102): two warm-up steps, then
+    per rep reset the peak counter, record the base allocation, run forward
+    through all blocks plus one autograd.grad, take peak - base; min over reps.
+    Block i's weights are seeded with seed 1 + i."""
+    import swiglu_recompute as SR
+    from oracle.swiglu_oracle import make_inputs
+
+    M, D, H = CFG["M"], CFG["D"], CFG["H"]
+    blocks = []
+    for i in range(n_blocks):
+        _, w1, w2, _ = make_inputs(1, D, H, D, seed=1 + i, dtype=torch.bfloat16)
+        b = SR.SwiGLUMLPCustom(D, H, D, dtype=torch.bfloat16).to(dev)
+        with torch.no_grad():
+            b.w1.copy_(w1)
+            b.w2.copy_(w2)
+        blocks.append(b)
+    model = torch.nn.Sequential(*blocks)
+    params = list(model.parameters())
+    x0, _, _, _ = make_inputs(M, D, 1, 1, seed=0, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(7)
+    x0 = x0.to(dev)
+    gout = torch.randn(M, D, generator=g).to(torch.bfloat16).to(dev)
+
+    def step():
+        x = x0.detach().requires_grad_(True)
+        y = model(x)
+        return torch.autograd.grad(y, [x] + params, gout)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(dev)
+        base = torch.cuda.memory_allocated(dev)
+        grads = step()
+        torch.cuda.synchronize()
+        peak = torch.cuda.max_memory_allocated(dev) - base
+        del grads
+        best = peak if best is None else min(best, peak)
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / iters)
+    del model, blocks, params
+    torch.cuda.empty_cache()
+    return best / 2 ** 20, min(times)
+
+
+def e2e_pipelined(model, params, x, gy, dev, args):
+    """Time `args.steps` steps through the public module API with host I/O.
+    Returns (ms per step, H2D bytes per step, D2H bytes per step)."""
+    M, D = x.shape
+    x_h = [x.clone().pin_memory() for _ in range(2)]
+    gy_h = [gy.clone().pin_memory() for _ in range(2)]
+    dx_h = [torch.empty((M, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    x_d = [torch.empty_like(x, device=dev) for _ in range(2)]
+    gy_d = [torch.empty_like(gy, device=dev) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+
+    def load(i):
+        s = i % 2
+        with torch.cuda.stream(copy):
+            copy.wait_event(consumed[s])
+            x_d[s].copy_(x_h[s], non_blocking=True)
+            gy_d[s].copy_(gy_h[s], non_blocking=True)
+            loaded[s].record(copy)
+
+    def run(nsteps):
+        for s in range(2):
+            consumed[s].record(comp)
+        load(0)
+        for i in range(nsteps):
+            s = i % 2
+            if i + 1 < nsteps:
+                load(i + 1)
+            comp.wait_event(loaded[s])
+            xi = x_d[s].requires_grad_(True)
+            gx = torch.autograd.grad(model(xi), [xi] + params, gy_d[s])[0]
+            x_d[s].requires_grad_(False)
+            done[s].record(comp)
+            with torch.cuda.stream(copy):
+                copy.wait_event(done[s])
+                dx_h[s].copy_(gx, non_blocking=True)
+                gx.record_stream(copy)
+            consumed[s].record(comp)
+
+    run(max(2, args.warmup // 2))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    run(args.steps)
+    comp.wait_stream(copy)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / args.steps, x.numel() * 2 + gy.numel() * 2, M * D * 2
+
+
 def run_ours_single(args):
     import swiglu_recompute as SR
     from swiglu_b200 import ops
@@ -287,30 +403,11 @@ def run_ours_single(args):
     fl = flops_fwd_bwd(M, D, H, Dout)
     value = fl / (ms * 1e-3) / 1e12
 
-    # End to end through the public API with host buffers.
-    x_h = x.pin_memory()
-    gy_h = gy.pin_memory()
-    dx_h = torch.empty((M, D), dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step():
-        xi = x_h.to(dev, non_blocking=True).requires_grad_(True)
-        gyi = gy_h.to(dev, non_blocking=True)
-        y = model(xi)
-        gx, gw1, gw2 = torch.autograd.grad(y, [xi] + params, gyi)
-        dx_h.copy_(gx, non_blocking=True)
-
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(st)
-    for _ in range(args.steps):
-        e2e_step()
-    e3.record(st)
-    torch.cuda.synchronize()
-    e2e_ms = e2.elapsed_time(e3) / args.steps
-    h2d = x_h.numel() * 2 + gy_h.numel() * 2
-    d2h = dx_h.numel() * 2
+    # End to end through the public API with host buffers: every step copies
+    # its x and grad_y in from pinned host memory and its grad_x out, on a copy
+    # stream that runs one step ahead (inputs of step i+1 and the output of
+    # step i move while step i+1 / i computes), as a data loader would.
+    e2e_ms, h2d, d2h = e2e_pipelined(model, params, x, gy, dev, args)
 
     # Per-kernel device times on the launching stream; dominant kernel roofline.
     w1d, w2d = model.w1.detach(), model.w2.detach()
@@ -335,11 +432,16 @@ def run_ours_single(args):
         "frac_of_peak": {"sustained": round(value / peak, 4),
                          "burst": round(value / float(peaks["bf16_tflops"]), 4), "source": peak_src},
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": profile_traffic(),
+                     "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": profile_traffic(dom),
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})"},
         "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
         "clocks": clk.summary(),
     }
+    if not args.no_stack:
+        peak, sms = stacked_depth(8, dev)
+        line["stacked"] = {"n_blocks": 8, "peak_mib": round(peak, 1), "ms_per_step": round(sms, 3),
+                           "reference_recompute_peak_mib": REFERENCE_STACK_PEAK_MIB[8],
+                           "method": "max_memory_allocated - base over fwd+grad, min of 3 (as the reference)"}
     if not args.no_cpu_baseline:
         tf, cores, sample = cpu_reference_sample(seconds=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
@@ -355,6 +457,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 8-block stacked-depth memory run")
     ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)
