@@ -271,7 +271,10 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
   // By size: pairs pay off once there is at least one full wave of them.
   if (mode == 0) mode = tiles2 >= d.sms / 2 ? 2 : 1;
   if (mode == 2) {
+    // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
+    // fused_forward.py:58); a pair tile covers two of them.
     p.tiles_m = (p.M + 255) / 256;
+    p.group_m = p.group_m > 1 ? p.group_m / 2 : 1;
     return launch_tc2<Tc2Cfg<A_MN, B_MN, EPI, F32>>(p, d, st);
   }
   p.tiles_m = (p.M + 127) / 128;

@@ -184,10 +184,30 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
       }
     }
   } else {  // kEpiDswiglu
+    // grad_h never leaves registers: each 32-column chunk of it is combined
+    // with the matching preact left/gate values and written back over them.
+    // The preact loads of chunk c+1 are issued before chunk c is computed so
+    // their latency hides behind the TMEM load and the SiLU math.
     const int j0 = pn * BN;
     __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
-#pragma unroll 1
+    uint4 lu[2][4], gu[2][4];
+    auto load_chunk = [&](int c, int buf) {
+      const int j = j0 + c * 32;
+      const int lc = left_col(j, p.H, p.layout);
+      const int gc = gate_col(j, p.H, p.layout);
+#pragma unroll
+      for (int v8 = 0; v8 < 4; ++v8) {
+        if (row_ok && j + 8 * v8 + 8 <= p.N) {
+          lu[buf][v8] = *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8);
+          gu[buf][v8] = *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8);
+        }
+      }
+    };
+    load_chunk(0, 0);
+#pragma unroll
     for (int c = 0; c < BN / 32; ++c) {
+      const int buf = c & 1;
+      if (c + 1 < BN / 32) load_chunk(c + 1, buf ^ 1);
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + c * 32, r);
       tmem_ld_wait();
@@ -198,11 +218,8 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
         float gl[32], gg[32];
 #pragma unroll
         for (int v8 = 0; v8 < 4; ++v8) {
-          if (j + 8 * v8 + 8 > p.N) continue;
-          const uint4 lu = *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8);
-          const uint4 gu = *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8);
-          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
-          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+          const uint32_t lw[4] = {lu[buf][v8].x, lu[buf][v8].y, lu[buf][v8].z, lu[buf][v8].w};
+          const uint32_t gw[4] = {gu[buf][v8].x, gu[buf][v8].y, gu[buf][v8].z, gu[buf][v8].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 l2 = unpack_bf16x2(lw[e]);
