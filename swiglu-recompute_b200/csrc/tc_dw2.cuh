@@ -283,10 +283,14 @@ struct Dw2PairCfg {
   static constexpr int B_BYTES = (BD / 2) * BK * 2;   // this CTA's grad_y columns
   static constexpr int STAGE_BYTES = A_BYTES + G_BYTES + B_BYTES;
   static constexpr int STAGES = 6;
-  // Two prologue warps per scheduler: the h recompute is latency- and
-  // issue-bound (ex2 + rcp per element); measured 1.66 -> 1.33 ms at
-  // M=11136 H=14336 Dout=3584 going from 4 to 8 warps.
+  // Prologue warps in groups, each group on its own ring slots; measured at
+  // M=11136 H=14336 Dout=3584: 4 warps on every stage 1.66 ms, 8 warps on
+  // every stage 1.33 ms, 2 groups of 4 warps 1.30 ms.
   static constexpr int NUM_XFORM_WARPS = 8;
+  static constexpr int XFORM_GROUPS = 2;
+  static constexpr int XFORM_THREADS_PER_GROUP = 32 * NUM_XFORM_WARPS / XFORM_GROUPS;
+  static_assert(STAGES % XFORM_GROUPS == 0, "each ring slot must belong to one prologue group");
+  static_assert(NUM_XFORM_WARPS % XFORM_GROUPS == 0, "equal prologue groups");
   static constexpr int NUM_THREADS = 32 * (2 + 4 + NUM_XFORM_WARPS);
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (4 * STAGES + 3) + 16;
@@ -317,7 +321,7 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&lg_full[s], 1);
       mbar_init(&b_full[s], 1);
-      mbar_init(&ready[s], 2 * C::NUM_XFORM_WARPS);
+      mbar_init(&ready[s], 2 * (C::NUM_XFORM_WARPS / C::XFORM_GROUPS));
       mbar_init(&empty[s], 1);
     }
     mbar_init(tmem_full, 1);
@@ -466,36 +470,46 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
       acc_phase ^= 1;
     }
   } else {
-    const uint32_t xt = threadIdx.x - 32 * 6;
+    // The prologue warps form C::XFORM_GROUPS groups and ring slot s belongs
+    // to group s % G (G divides STAGES), so G stages are transformed
+    // concurrently (per-stage latency, not the math rate, limits a single
+    // stage in flight). Owning whole slots keeps the parity protocol exact: a
+    // group waits on every phase of its slots in order, so a parity test can
+    // never match a phase two generations old.
+    const uint32_t xw = threadIdx.x - 32 * 6;
+    const uint32_t grp = xw / C::XFORM_THREADS_PER_GROUP;
+    const uint32_t xt = xw % C::XFORM_THREADS_PER_GROUP;
     constexpr int kChunks = C::A_BYTES / 16;
     uint32_t stage = 0, phase = 0;
     bool ok = true;
     for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
       for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&lg_full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
-          ok = false;
-          break;
-        }
-        uint4* sa = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
-        const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * C::STAGE_BYTES + C::A_BYTES);
-#pragma unroll
-        for (int i = static_cast<int>(xt); i < kChunks; i += 32 * C::NUM_XFORM_WARPS) {
-          const uint4 lu = sa[i];
-          const uint4 gu = sg[i];
-          const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
-          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-          uint32_t hw[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 l2 = unpack_bf16x2(lw[e]);
-            const float2 g2 = unpack_bf16x2(gw[e]);
-            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
+        if (stage % C::XFORM_GROUPS == grp) {
+          if (!mbar_wait(&lg_full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
+            ok = false;
+            break;
           }
-          sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          uint4* sa = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
+          const uint4* sg = reinterpret_cast<const uint4*>(smem + stage * C::STAGE_BYTES + C::A_BYTES);
+#pragma unroll
+          for (int i = static_cast<int>(xt); i < kChunks; i += C::XFORM_THREADS_PER_GROUP) {
+            const uint4 lu = sa[i];
+            const uint4 gu = sg[i];
+            const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+            const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+            uint32_t hw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 l2 = unpack_bf16x2(lw[e]);
+              const float2 g2 = unpack_bf16x2(gw[e]);
+              hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
+            }
+            sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(map_to_rank(&ready[stage], 0));
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(map_to_rank(&ready[stage], 0));
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
