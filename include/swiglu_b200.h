@@ -96,6 +96,31 @@ int swiglu_b200_fused_matmul_swiglu_save_preact(const void* x, const void* w, vo
 int swiglu_b200_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout,
                        int b_layout, int dtype, int out_dtype, int group_size_m, void* stream);
 
+/* Tensor-parallel reduce-scatter fused into a GEMM (used for the partial y
+ * and grad_x of the tensor-parallel block). The f32 result D [M, N] =
+ * op(A) . op(B) is not stored locally: row r goes to rank o = r / rows_per_rank,
+ * into peer_bufs[o] (a device pointer valid on this GPU, usually another GPU's
+ * memory mapped over NVLink) at row rank * rows_per_rank + r % rows_per_rank of
+ * a [world * rows_per_rank, N] f32 receive buffer. peer_bufs is a host array of
+ * `world` pointers; M == world * rows_per_rank; bf16 operands; world <= 8.
+ * Replaces the NCCL reduce-scatter after `h @ W2.t()` / `grad_preact @ W1` of a
+ * tensor-parallel block (the reference is single-GPU; the math per rank is
+ * swiglu_recompute.py:65,77). */
+int swiglu_b200_matmul_scatter_rows(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int a_layout,
+                                    int b_layout, int dtype, void* const* peer_bufs, int world, int rank,
+                                    int64_t rows_per_rank, void* stream);
+
+/* After the preceding work on `stream`: publishes `epoch` into
+ * peer_flags[o][rank] for every owner o (peer_flags: host array of `world`
+ * device pointers to each rank's flag array of `world` uint32). */
+int swiglu_b200_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint32_t epoch, void* stream);
+
+/* Owner side: waits (bounded; timeout sets a device status bit) until
+ * flags[s] == epoch for every source s, then out [rows, N] = sum over
+ * s = 0..world-1 of recv[s] [rows, N] in that order (f32), stored as out_dtype. */
+int swiglu_b200_tp_reduce_rows(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out,
+                               int64_t rows, int64_t N, int out_dtype, void* stream);
+
 /* dW2 [Dout, H] = grad_y^T . h with h = left * silu(gate) recomputed from preact
  * inside the GEMM's operand prologue (no [M, H] buffer).
  * Replaces `h = _swiglu_forward_logic(preact); grad_W2 = grad_y.t() @ h`

@@ -440,6 +440,106 @@ int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64
 #undef SWIGLU_MM
 }
 
+int op_matmul_scatter(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int a_layout, int b_layout,
+                      int dtype, void* const* peer_bufs, int world, int rank, int64_t rows_per_rank,
+                      cudaStream_t st) {
+  if (int rc = check_dims("matmul_scatter_rows", M, N, K)) return rc;
+  if (dtype != SWIGLU_BF16) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "the scatter GEMM takes bf16 operands");
+  if ((a_layout | b_layout) & ~1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "layout flags must be 0 or 1");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "world must be 1..8 and 0 <= rank < world");
+  if (rows_per_rank <= 0 || rows_per_rank * world != M)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "M=%lld must equal world*rows_per_rank", (long long)M);
+  if (K <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K must be positive");
+  if (!a || !b || !peer_bufs) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  for (int i = 0; i < world; ++i) {
+    if (!peer_bufs[i] || reinterpret_cast<uintptr_t>(peer_bufs[i]) % 16)
+      return fail(SWIGLU_ERR_MISALIGNED, "peer buffer %d is null or not 16-byte aligned", i);
+  }
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  const bool a_mn = a_layout == 1, b_mn = b_layout == 0;
+  if (!a_mn || !b_mn) { if (int rc = check_mult8("K", K)) return rc; }
+  if (a_mn) { if (int rc = check_mult8("M", M)) return rc; }
+  if (int rc = check_mult8("N", N)) return rc;
+  TcParams p{};
+  if (a_mn) {
+    if (int rc = map_mnmajor(&p.tmA, a, K, M, M, "A")) return rc;
+  } else {
+    if (int rc = map_kmajor(&p.tmA, a, M, K, K, 128, "A")) return rc;
+  }
+  if (b_mn) {
+    if (int rc = map_mnmajor(&p.tmB, b, K, N, N, "B")) return rc;
+  } else {
+    if (int rc = map_kmajor(&p.tmB, b, N, K, K, 128, "B")) return rc;
+  }
+  for (int i = 0; i < world; ++i) p.peer[i] = static_cast<float*>(peer_bufs[i]);
+  p.rows_per_rank = (int)rows_per_rank;
+  p.src_rank = rank;
+  p.ld0 = N;
+  p.M = (int)M, p.N = (int)N, p.K = (int)K;
+  p.tiles_n = (int)((N + 255) / 256);
+  p.group_m = 16;
+  if (a_mn) return b_mn ? run_gemm<true, true, kEpiScatterRows, true>(p, *d, st)
+                        : run_gemm<true, false, kEpiScatterRows, true>(p, *d, st);
+  return b_mn ? run_gemm<false, true, kEpiScatterRows, true>(p, *d, st)
+              : run_gemm<false, false, kEpiScatterRows, true>(p, *d, st);
+}
+
+struct PeerFlags {
+  uint32_t* f[8];
+};
+
+__global__ void tp_signal_param_kernel(PeerFlags pf, int world, int rank, uint32_t epoch) {
+  const int o = threadIdx.x;
+  if (o < world) {
+    __threadfence_system();
+    volatile uint32_t* f = pf.f[o] + rank;
+    *f = epoch;
+    __threadfence_system();
+  }
+}
+
+int op_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint32_t epoch, cudaStream_t st) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "world must be 1..8 and 0 <= rank < world");
+  if (!peer_flags) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  PeerFlags pf{};
+  for (int i = 0; i < world; ++i) {
+    if (!peer_flags[i]) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null flag pointer %d", i);
+    pf.f[i] = peer_flags[i];
+  }
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  tp_signal_param_kernel<<<1, 32, 0, st>>>(pf, world, rank, epoch);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "tp_signal launch");
+}
+
+int op_tp_reduce(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out, int64_t rows,
+                 int64_t N, int out_dtype, cudaStream_t st) {
+  if (int rc = check_dims("tp_reduce_rows", rows, N, world)) return rc;
+  if (world < 1 || world > 8) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "world must be 1..8");
+  if (int rc = check_dtype(out_dtype)) return rc;
+  if (N % 4) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "N=%lld must be a multiple of 4", (long long)N);
+  if (!recv || !flags || !out) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(recv) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "recv/out must be 16-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  if (rows == 0 || N == 0) return SWIGLU_OK;
+  const int grid = pointwise_grid(rows * (N / 4), *d);
+  if (out_dtype == SWIGLU_F32)
+    tp_reduce_rows_kernel<float><<<grid, 256, 0, st>>>(recv, flags, world, epoch, static_cast<float*>(out), rows,
+                                                       (int)N, d->status);
+  else
+    tp_reduce_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(recv, flags, world, epoch,
+                                                               static_cast<__nv_bfloat16*>(out), rows, (int)N,
+                                                               d->status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "tp_reduce launch");
+}
+
 int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, int64_t Dout, int dtype, int layout,
            cudaStream_t st) {
   if (int rc = check_dims("bwd_dw2", M, 2 * H, Dout)) return rc;
@@ -626,6 +726,22 @@ int swiglu_b200_device_status(uint32_t* bits, int clear) {
   }
   *bits = v;
   return v ? fail(SWIGLU_ERR_DEVICE_TIMEOUT, "kernel pipeline wait timed out (bits 0x%x)", v) : SWIGLU_OK;
+}
+
+int swiglu_b200_matmul_scatter_rows(const void* a, const void* b, int64_t M, int64_t N, int64_t K, int a_layout,
+                                    int b_layout, int dtype, void* const* peer_bufs, int world, int rank,
+                                    int64_t rows_per_rank, void* stream) {
+  return op_matmul_scatter(a, b, M, N, K, a_layout, b_layout, dtype, peer_bufs, world, rank, rows_per_rank,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint32_t epoch, void* stream) {
+  return op_tp_signal(peer_flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_tp_reduce_rows(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out,
+                               int64_t rows, int64_t N, int out_dtype, void* stream) {
+  return op_tp_reduce(recv, flags, world, epoch, out, rows, N, out_dtype, static_cast<cudaStream_t>(stream));
 }
 
 int swiglu_b200_set_gemm_path(int mode) {

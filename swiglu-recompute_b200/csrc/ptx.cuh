@@ -21,6 +21,7 @@ enum : uint32_t {
   kErrTimeoutEpilogue = 1u << 2,
   kErrTimeoutTransform = 1u << 3,
   kErrTimeoutTeardown = 1u << 4,
+  kErrTimeoutPeer = 1u << 5,  // a peer rank's tensor-parallel signal never arrived
 };
 
 // 2 s: many orders of magnitude above any legitimate wait (one k-block of one

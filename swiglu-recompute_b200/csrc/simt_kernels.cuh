@@ -247,4 +247,53 @@ __global__ void pack_chunked_kernel(const T* __restrict__ src, T* __restrict__ d
   }
 }
 
+// ------------------------------------------- tensor-parallel reduce-scatter
+// Owner side: wait until every source published `epoch` (bounded), then
+// out[i, j] = sum over s = 0..world-1 of recv[s, i, j] in that fixed order.
+template <typename OutT>
+__global__ void tp_reduce_rows_kernel(const float* __restrict__ recv, const uint32_t* flags, int world,
+                                      uint32_t epoch, OutT* __restrict__ out, long long rows, int n,
+                                      uint32_t* status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t deadline = global_timer_ns() + 2ull * kWaitTimeoutNs;
+    for (int s = 0; s < world; ++s) {
+      const volatile uint32_t* f = flags + s;
+      while (*f != epoch) {
+        if (global_timer_ns() > deadline) {
+          if (status) atomicOr(status, kErrTimeoutPeer);
+          ok = 0;
+          break;
+        }
+      }
+      if (!ok) break;
+    }
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (!ok) return;
+  const long long total4 = rows * (n / 4);
+  const long long slab = rows * static_cast<long long>(n);
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total4;
+       e += (long long)gridDim.x * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(recv)[e];
+    for (int s = 1; s < world; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(recv + s * slab)[e];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if constexpr (sizeof(OutT) == 4) {
+      reinterpret_cast<float4*>(out)[e] = acc;
+    } else {
+      uint2 u;
+      u.x = pack_bf16x2(acc.x, acc.y);
+      u.y = pack_bf16x2(acc.z, acc.w);
+      reinterpret_cast<uint2*>(out)[e] = u;
+    }
+  }
+}
+
 }  // namespace swiglu

@@ -34,7 +34,7 @@
 
 namespace swiglu {
 
-enum EpiKind : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiDswiglu = 2 };
+enum EpiKind : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiDswiglu = 2, kEpiScatterRows = 3 };
 enum Layout : int { kLayoutStd = 0, kLayoutPacked = 1 };
 
 constexpr int kPackChunk = 128;  // BLOCK_SIZE_N_HALF of the packed layout (fused_forward_packed.py:41)
@@ -63,7 +63,16 @@ struct TcParams {
   uint32_t mn_lbo;  // MN-major operands: byte offset between 64-element MN blocks
   uint32_t mn_sbo;  // MN-major operands: byte offset between 8-row K groups
   uint32_t* status; // device error word
+  // kEpiScatterRows: f32 row r of D goes to rank r / rows_per_rank's buffer
+  // peer[r / rows_per_rank], at row src_rank * rows_per_rank + r % rows_per_rank
+  // (row pitch ld0). The buffers may be other GPUs' memory (NVLink P2P).
+  float* peer[8];
+  int rows_per_rank, src_rank;
 };
+
+// Shared-memory staging per epilogue warp for kEpiScatterRows: a 32 x 32 f32
+// block with a 33-float row pitch (bank-conflict-free both ways).
+constexpr int kScatterStageFloats = 32 * 33;
 
 constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
 
@@ -86,7 +95,8 @@ struct TcCfg {
   static constexpr int NUM_EPI_WARPS = 4;
   static constexpr int NUM_THREADS = 32 * (2 + NUM_EPI_WARPS);
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? NUM_EPI_WARPS * kScatterStageFloats * 4 : 0;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + EPI_STAGE_BYTES;
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
   static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
@@ -135,7 +145,8 @@ __device__ __forceinline__ void store_row32(void* row_ptr, int c0, int ncols, co
 // output (this thread's TMEM lane) and its TMEM address `t_row` (lane base +
 // accumulator column base). Tile (pm, pn) of BN accumulator columns.
 template <int BN, int EPI, bool OUT_F32>
-__device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn, int row, uint32_t t_row) {
+__device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn, int row, uint32_t t_row,
+                                              float* stage = nullptr) {
   const bool row_ok = row < p.M;
   if constexpr (EPI == kEpiStore) {
     const int n0 = pn * BN;
@@ -182,6 +193,39 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
         store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
         if (h_row) store_row32<false>(h_row, j, p.N, hf);
       }
+    }
+  } else if constexpr (EPI == kEpiScatterRows) {
+    // Tensor-parallel reduce-scatter fused into the GEMM: each f32 partial
+    // row goes straight into its owning rank's receive slot, usually another
+    // GPU's memory. Each 32 x 32 block is transposed through shared memory so
+    // that a warp store writes four whole 128-byte row segments (lane l: row
+    // 4i + l/8, columns 4(l%8)..+3) instead of 16 bytes of 32 different rows.
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    const int row0 = row - lane;  // first row of this warp's 32-row group
+    const int n0 = pn * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = __uint_as_float(r[i]);
+      __syncwarp();
+      const int col = n0 + c * 32 + 4 * (lane & 7);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = 4 * i + (lane >> 3);
+        const int grow = row0 + rr;
+        if (grow < p.M && col + 4 <= p.N) {
+          const int owner = grow / p.rows_per_rank;
+          const long long dst_row =
+              static_cast<long long>(p.src_rank) * p.rows_per_rank + (grow - owner * p.rows_per_rank);
+          const float* src = stage + rr * 33 + 4 * (lane & 7);
+          *reinterpret_cast<float4*>(p.peer[owner] + dst_row * p.ld0 + col) =
+              make_float4(src[0], src[1], src[2], src[3]);
+        }
+      }
+      __syncwarp();
     }
   } else {  // kEpiDswiglu
     // grad_h never leaves registers: each 32-column chunk of it is combined
@@ -414,8 +458,9 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm_kernel(const __gr
       tc_fence_after_sync();
       const int row = pm * BM + static_cast<int>(q * 32 + lane);
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-
-      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row);
+      float* stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES) +
+                     (warp - 2) * kScatterStageFloats;
+      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[acc]);

@@ -40,7 +40,9 @@ struct Tc2Cfg {
   static constexpr int STAGES = 6;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int NUM_THREADS = 192;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5) + 16;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4 : 0;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + EPI_STAGE_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -200,7 +202,9 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       tc_fence_after_sync();
       const int row = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row);
+      float* stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES) +
+                     (warp - 2) * kScatterStageFloats;
+      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[acc], 0));

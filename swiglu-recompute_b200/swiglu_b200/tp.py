@@ -22,6 +22,7 @@ SwiGLUMemoryOptimizedFunction, swiglu_recompute.py:58-78).
 """
 from __future__ import annotations
 
+import ctypes
 import os
 import time
 from datetime import timedelta
@@ -74,6 +75,69 @@ def reduce_scatter_rows(t: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+# ------------------------------------------- fused GEMM -> reduce-scatter
+class FusedReduceScatter:
+    """Receive buffers in symmetric (peer-mapped) memory for the reduce-scatter
+    of an f32 partial product, fused into the producing GEMM.
+
+    For a partial D [M, N] on every rank (M = world * rows_per_rank), the GEMM
+    epilogue stores row r into rank r // rows_per_rank's receive buffer
+    [world, rows_per_rank, N] at slot [this rank, r % rows_per_rank] over
+    NVLink while the other tiles are still computing; a signal kernel then
+    publishes the call's epoch into every owner's flag slot for this rank, and
+    each owner sums its `world` slots in fixed rank order (deterministic) and
+    rounds once. Buffers are reused across calls: between two uses of the
+    same buffer every rank passes through other collectives of the step, which
+    orders the next writes after the previous reduction.
+    """
+
+    def __init__(self, group=None):
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.epoch = 0
+        self._slots = {}
+
+    def _slot(self, key, rows_per_rank, n, device):
+        k = (key, rows_per_rank, n)
+        if k not in self._slots:
+            import torch.distributed._symmetric_memory as symm_mem
+            recv = symm_mem.empty(self.world * rows_per_rank * n, dtype=torch.float32, device=device)
+            recv_h = symm_mem.rendezvous(recv, self.group)
+            flags = symm_mem.empty(self.world, dtype=torch.int32, device=device)
+            flags.zero_()
+            flags_h = symm_mem.rendezvous(flags, self.group)
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.group)
+            peers = (ctypes.c_void_p * self.world)(*[recv_h.buffer_ptrs[i] for i in range(self.world)])
+            peer_flags = (ctypes.c_void_p * self.world)(*[flags_h.buffer_ptrs[i] for i in range(self.world)])
+            self._slots[k] = (recv, recv_h, flags, flags_h, peers, peer_flags)
+        return self._slots[k]
+
+    def matmul(self, key, a, b, *, a_t, b_t, out_dtype):
+        """Reduce-scattered op(a) . op(b): returns this rank's [M / world, N] rows."""
+        from ._lib import BF16, call
+        from .ops import _p, _stream, dtype_code
+
+        M = a.shape[1] if a_t else a.shape[0]
+        K = a.shape[0] if a_t else a.shape[1]
+        N = b.shape[0] if b_t else b.shape[1]
+        assert M % self.world == 0
+        rows = M // self.world
+        dev = a.device
+        recv, _, flags, _, peers, peer_flags = self._slot(key, rows, N, dev)
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        out = torch.empty((rows, N), device=dev, dtype=out_dtype)
+        st = _stream(dev)
+        with torch.cuda.device(dev):
+            call("swiglu_b200_matmul_scatter_rows", _p(a), _p(b), M, N, K, int(a_t), int(b_t), BF16,
+                 peers, self.world, self.rank, rows, st)
+            call("swiglu_b200_tp_signal", peer_flags, self.world, self.rank, self.epoch, st)
+            call("swiglu_b200_tp_reduce_rows", _p(recv), _p(flags), self.world, self.epoch, _p(out), rows, N,
+                 dtype_code(out_dtype), st)
+        return out
+
+
 # -------------------------------------------------------- local compute
 class NativeCompute:
     """Per-rank compute on libswiglu_b200.so (bf16 tcgen05 or f32 kernels)."""
@@ -97,15 +161,18 @@ class NativeCompute:
 
 class _TPSwiGLUFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32):
+    def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs):
         x = all_gather_rows(x_local, group)
         preact, h = compute.swiglu_fwd(x, w1_local)
-        acc_dt = torch.float32 if reduce_f32 else x.dtype
-        y_part = compute.matmul(h, w2_local, a_t=False, b_t=True, out_dtype=acc_dt)
+        if fused_rs is not None:
+            y_local = fused_rs.matmul("y", h, w2_local, a_t=False, b_t=True, out_dtype=x.dtype)
+        else:
+            acc_dt = torch.float32 if reduce_f32 else x.dtype
+            y_part = compute.matmul(h, w2_local, a_t=False, b_t=True, out_dtype=acc_dt)
+            y_local = reduce_scatter_rows(y_part, group).to(x.dtype)
         del h
-        y_local = reduce_scatter_rows(y_part, group).to(x.dtype)
         ctx.save_for_backward(x, w1_local, w2_local, preact)
-        ctx.group, ctx.compute, ctx.reduce_f32 = group, compute, reduce_f32
+        ctx.group, ctx.compute, ctx.reduce_f32, ctx.fused_rs = group, compute, reduce_f32, fused_rs
         return y_local
 
     @staticmethod
@@ -120,15 +187,20 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         gp = compute.grad_preact_inplace(gy, w2_local, preact)
         torch.autograd.graph.increment_version(preact)
         dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
-        acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
-        dx_part = compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt)
-        dx_local = reduce_scatter_rows(dx_part, ctx.group).to(x.dtype)
-        return dx_local, dw1, dw2, None, None, None
+        if ctx.fused_rs is not None:
+            dx_local = ctx.fused_rs.matmul("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
+        else:
+            acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
+            dx_part = compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt)
+            dx_local = reduce_scatter_rows(dx_part, ctx.group).to(x.dtype)
+        return dx_local, dw1, dw2, None, None, None, None
 
 
-def tp_swiglu(x_local, w1_local, w2_local, group=None, compute=NativeCompute, reduce_f32=True):
-    """y_r [M/t, Dout] for the token shard x_r [M/t, D]; see the module docstring."""
-    return _TPSwiGLUFunction.apply(x_local, w1_local, w2_local, group, compute, reduce_f32)
+def tp_swiglu(x_local, w1_local, w2_local, group=None, compute=NativeCompute, reduce_f32=True, fused_rs=None):
+    """y_r [M/t, Dout] for the token shard x_r [M/t, D]; see the module docstring.
+    With `fused_rs` (a FusedReduceScatter) the reduce-scatters of y and grad_x
+    run inside their GEMMs over NVLink instead of as NCCL collectives."""
+    return _TPSwiGLUFunction.apply(x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs)
 
 
 class SwiGLUMLPTensorParallel(nn.Module):
@@ -136,9 +208,12 @@ class SwiGLUMLPTensorParallel(nn.Module):
     rank's shards: w1 [2H/t, D], w2 [Dout, H/t])."""
 
     def __init__(self, dim, hidden_dim, out_dim=None, dtype=torch.float32, group=None,
-                 reduce_f32=True):
+                 reduce_f32=True, fused_rs=None):
         super().__init__()
         self.group = group
+        # Fused GEMM + reduce-scatter over NVLink (bf16 only); default on for
+        # bf16 when CUDA peer memory is available.
+        self.fused_rs = fused_rs
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         assert hidden_dim % self.world == 0
@@ -156,7 +231,12 @@ class SwiGLUMLPTensorParallel(nn.Module):
         return self
 
     def forward(self, x_local):
-        return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32)
+        frs = None
+        if self.fused_rs is not False and x_local.dtype == torch.bfloat16 and x_local.is_cuda:
+            if self.fused_rs is None or self.fused_rs is True:
+                self.fused_rs = FusedReduceScatter(self.group)
+            frs = self.fused_rs
+        return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32, frs)
 
 
 # -------------------------------------------------------------- bench
@@ -177,7 +257,9 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
         assert M % world == 0 and H % world == 0
         x, w1, w2, gy = make_inputs(M, D, H, Dout, seed=0, dtype=torch.bfloat16)
         ms_rows = M // world
-        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16).to(dev).load_full(w1, w2)
+        fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
+        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
+                                        fused_rs=None if fused else False).to(dev).load_full(w1, w2)
         params = list(model.parameters())
         x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
         gy_l = gy[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
@@ -246,7 +328,9 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": "cfg2: one SwiGLU MLP block fwd+bwd, tensor parallel", **cfg,
-                       "parallelism": f"tp{world}", "reduce": "f32 partials, NCCL reduce-scatter",
+                       "parallelism": f"tp{world}",
+                       "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
+                                  if fused else "f32 partials, NCCL reduce-scatter"),
                        "l2": "working set > L2"},
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),

@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shape, q):
+def _worker(rank, world, port, shape, fused, q):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -38,10 +38,14 @@ def _worker(rank, world, port, shape, q):
         M, D, H, Dout = shape
         x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=11, dtype=torch.bfloat16)
         ms = M // world
-        mlp = tp.SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16).to(dev).load_full(w1, w2)
+        mlp = tp.SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
+                                         fused_rs=None if fused else False).to(dev).load_full(w1, w2)
         xl = x[rank * ms:(rank + 1) * ms].to(dev).requires_grad_(True)
         y = mlp(xl)
         dx, dw1, dw2 = torch.autograd.grad(y, [xl, mlp.w1, mlp.w2], gy[rank * ms:(rank + 1) * ms].to(dev))
+        # a second step through the same buffers (epoch advance, buffer reuse)
+        y2 = mlp(xl.detach().requires_grad_(True))
+        assert torch.equal(y2.detach(), y.detach())
         outs = [y.detach(), dx, dw1, dw2]
         gathered = []
         for t in outs:
@@ -55,8 +59,9 @@ def _worker(rank, world, port, shape, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused_rs", "nccl_rs"])
 @pytest.mark.parametrize("world", [2])
-def test_tensor_parallel_matches_oracle(world):
+def test_tensor_parallel_matches_oracle(world, fused):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from swiglu_b200 import tp
@@ -65,7 +70,7 @@ def test_tensor_parallel_matches_oracle(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fused, q)) for r in range(world)]
     for p in procs:
         p.start()
     ys, dxs, dw1s, dw2s = q.get(timeout=300)
