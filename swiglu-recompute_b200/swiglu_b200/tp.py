@@ -114,6 +114,16 @@ class FusedReduceScatter:
             self._slots[k] = (recv, recv_h, flags, flags_h, peers, peer_flags)
         return self._slots[k]
 
+    # Fused only when the GEMM's math covers its NVLink push: per rank the
+    # GEMM takes ~2MNK / 1.3 PFLOP/s while (world-1)/world of its 4MN bytes
+    # leave at ~0.6 TB/s, i.e. K >= 4333 (world-1) / world. Measured at
+    # config 2 (M=11136): world 2 fused 4.60 ms/step vs NCCL 4.96; world 8
+    # (y: K=1792, dx: K=3584) fused 2.18 vs NCCL 2.05.
+    K_PER_LINK_BYTE = 4333
+
+    def wants(self, k):
+        return k * self.world >= self.K_PER_LINK_BYTE * (self.world - 1)
+
     def matmul(self, key, a, b, *, a_t, b_t, out_dtype):
         """Reduce-scattered op(a) . op(b): returns this rank's [M / world, N] rows."""
         from ._lib import BF16, call
@@ -164,7 +174,7 @@ class _TPSwiGLUFunction(torch.autograd.Function):
     def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs):
         x = all_gather_rows(x_local, group)
         preact, h = compute.swiglu_fwd(x, w1_local)
-        if fused_rs is not None:
+        if fused_rs is not None and fused_rs.wants(h.shape[1]):
             y_local = fused_rs.matmul("y", h, w2_local, a_t=False, b_t=True, out_dtype=x.dtype)
         else:
             acc_dt = torch.float32 if reduce_f32 else x.dtype
@@ -187,7 +197,7 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         gp = compute.grad_preact_inplace(gy, w2_local, preact)
         torch.autograd.graph.increment_version(preact)
         dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
-        if ctx.fused_rs is not None:
+        if ctx.fused_rs is not None and ctx.fused_rs.wants(gp.shape[1]):
             dx_local = ctx.fused_rs.matmul("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
         else:
             acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype

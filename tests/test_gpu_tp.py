@@ -38,8 +38,12 @@ def _worker(rank, world, port, shape, fused, q):
         M, D, H, Dout = shape
         x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=11, dtype=torch.bfloat16)
         ms = M // world
+        frs = None
+        if fused:
+            frs = tp.FusedReduceScatter()
+            frs.K_PER_LINK_BYTE = 0          # always fuse at this small test shape
         mlp = tp.SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
-                                         fused_rs=None if fused else False).to(dev).load_full(w1, w2)
+                                         fused_rs=frs if fused else False).to(dev).load_full(w1, w2)
         xl = x[rank * ms:(rank + 1) * ms].to(dev).requires_grad_(True)
         y = mlp(xl)
         dx, dw1, dw2 = torch.autograd.grad(y, [xl, mlp.w1, mlp.w2], gy[rank * ms:(rank + 1) * ms].to(dev))
