@@ -121,6 +121,23 @@ int swiglu_b200_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint
 int swiglu_b200_tp_reduce_rows(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out,
                                int64_t rows, int64_t N, int out_dtype, void* stream);
 
+/* The tensor-parallel GEMM -> reduce pipeline above for a single rank
+ * (matmul_scatter_rows + tp_signal + tp_reduce_rows with world = 1), for callers
+ * that cannot allocate device memory: code embedded in a host application
+ * whose own pool owns the whole device and forbids cudaMalloc, or code on a
+ * path where cudaMalloc's implicit device synchronisation is not allowed.
+ * Computes out [M, N] = op(A) . op(B) (bf16 operands, f32 accumulation,
+ * out_dtype result) through the library's static device scratch instead of a
+ * caller-provided receive buffer; no device memory is allocated.
+ * Limit: M * N <= 4,194,304 (16 MiB of f32 scratch, held on every GPU that
+ * loads the library until the process exits); larger sizes are rejected with
+ * SWIGLU_ERR_INVALID_ARGUMENT. All calls share that scratch: calls that
+ * overlap on the GPU (e.g. on different streams) race. The first call on a
+ * device resolves the scratch address for that device; make that first call
+ * before any stream capture. No counterpart in the reference. */
+int swiglu_b200_matmul_reduce_rows_noalloc(const void* a, const void* b, void* out, int64_t M, int64_t N,
+                                           int64_t K, int a_layout, int b_layout, int out_dtype, void* stream);
+
 /* dW2 [Dout, H] = grad_y^T . h with h = left * silu(gate) recomputed from preact
  * inside the GEMM's operand prologue (no [M, H] buffer).
  * Replaces `h = _swiglu_forward_logic(preact); grad_W2 = grad_y.t() @ h`

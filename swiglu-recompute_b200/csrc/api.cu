@@ -688,6 +688,64 @@ int op_pack(const void* src, void* dst, int64_t K, int64_t Nh, int64_t B, int dt
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "pack launch");
 }
 
+// ------------------------------------------------ no-allocation variant
+// The single-rank form of the fused reduce-scatter pipeline (scatter GEMM ->
+// signal -> reduce) with its receive buffer and flags in file-scope device
+// arrays instead of caller memory. The arrays live on every GPU that loads
+// this library until the process exits; every call shares them.
+constexpr long long kNoAllocScratchFloats = 4ll << 20;  // 16 MiB of f32: M * N <= 4,194,304
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) uint32_t g_noalloc_flags[8];
+
+struct NoAllocState {
+  std::atomic<bool> ready{false};
+  float* scratch = nullptr;
+  uint32_t* flags = nullptr;
+  std::atomic<uint32_t> epoch{0};
+};
+NoAllocState g_noalloc[kMaxDevices];
+
+int op_matmul_reduce_noalloc(const void* a, const void* b, void* out, int64_t M, int64_t N, int64_t K,
+                             int a_layout, int b_layout, int out_dtype, cudaStream_t st) {
+  if (int rc = check_dims("matmul_reduce_rows_noalloc", M, N, K)) return rc;
+  if (M * N > kNoAllocScratchFloats)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT,
+                "matmul_reduce_rows_noalloc: M*N=%lld exceeds the static scratch of %lld floats (16 MiB)",
+                (long long)(M * N), kNoAllocScratchFloats);
+  if (M == 0 || N == 0) return SWIGLU_OK;
+  if (!out) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  NoAllocState& s = g_noalloc[dev];
+  if (!s.ready.load(std::memory_order_acquire)) {
+    // Set-up, once per device, with that device current: resolve the device
+    // addresses of the static arrays (their host-side names are not device
+    // addresses).
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!s.ready.load(std::memory_order_relaxed)) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+      s.scratch = static_cast<float*>(p);
+      e = cudaGetSymbolAddress(&p, g_noalloc_flags);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc flags)");
+      s.flags = static_cast<uint32_t*>(p);
+      s.ready.store(true, std::memory_order_release);
+    }
+  }
+  // The flags keep the previous call's value; a fresh epoch per call means
+  // nothing has to be cleared (the GEMM overwrites all M*N scratch floats).
+  uint32_t epoch = s.epoch.fetch_add(1) + 1;
+  if (epoch == 0) epoch = s.epoch.fetch_add(1) + 1;
+  void* peers[1] = {s.scratch};
+  if (int rc = op_matmul_scatter(a, b, M, N, K, a_layout, b_layout, SWIGLU_BF16, peers, 1, 0, M, st)) return rc;
+  uint32_t* flag_ptrs[1] = {s.flags};
+  if (int rc = op_tp_signal(flag_ptrs, 1, 0, epoch, st)) return rc;
+  return op_tp_reduce(s.scratch, s.flags, 1, epoch, out, M, N, out_dtype, st);
+}
+
 }  // namespace
 }  // namespace swiglu
 
@@ -742,6 +800,12 @@ int swiglu_b200_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint
 int swiglu_b200_tp_reduce_rows(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out,
                                int64_t rows, int64_t N, int out_dtype, void* stream) {
   return op_tp_reduce(recv, flags, world, epoch, out, rows, N, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_matmul_reduce_rows_noalloc(const void* a, const void* b, void* out, int64_t M, int64_t N,
+                                           int64_t K, int a_layout, int b_layout, int out_dtype, void* stream) {
+  return op_matmul_reduce_noalloc(a, b, out, M, N, K, a_layout, b_layout, out_dtype,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 int swiglu_b200_set_gemm_path(int mode) {

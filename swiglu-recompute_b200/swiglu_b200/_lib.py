@@ -37,6 +37,7 @@ _SIGNATURES = {
         [_p, _p, _i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_p), _i, _i, _i64, _p],
     "swiglu_b200_tp_signal": [ctypes.POINTER(_p), _i, _i, ctypes.c_uint32, _p],
     "swiglu_b200_tp_reduce_rows": [_p, _p, _i, ctypes.c_uint32, _p, _i64, _i64, _i, _p],
+    "swiglu_b200_matmul_reduce_rows_noalloc": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p],
     "swiglu_b200_bwd_dw2": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
     "swiglu_b200_bwd_grad_preact_inplace": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
     "swiglu_b200_forward_logic": [_p, _p, _i64, _i64, _i, _i, _p],
