@@ -252,7 +252,7 @@ def run_kernel_only(args):
 REFERENCE_STACK_PEAK_MIB = {1: 2275, 2: 2961, 4: 4334, 8: 7078, 16: 12567}   # results_b200.md:38-42
 
 
-def stacked_depth(n_blocks, dev, reps=3, iters=3):
+def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom"):
     """Peak allocated-memory delta (MiB) and ms per fwd+bwd of `n_blocks`
     stacked config-2 blocks, measured as the reference's stacked-depth
     benchmark does (bench_stacked_blocks.py:55-102): two warm-up steps, then
@@ -266,7 +266,7 @@ def stacked_depth(n_blocks, dev, reps=3, iters=3):
     blocks = []
     for i in range(n_blocks):
         _, w1, w2, _ = make_inputs(1, D, H, D, seed=1 + i, dtype=torch.bfloat16)
-        b = SR.SwiGLUMLPCustom(D, H, D, dtype=torch.bfloat16).to(dev)
+        b = getattr(SR, module)(D, H, D, dtype=torch.bfloat16).to(dev)
         with torch.no_grad():
             b.w1.copy_(w1)
             b.w2.copy_(w2)
@@ -442,6 +442,9 @@ def run_ours_single(args):
         line["stacked"] = {"n_blocks": 8, "peak_mib": round(peak, 1), "ms_per_step": round(sms, 3),
                            "reference_recompute_peak_mib": REFERENCE_STACK_PEAK_MIB[8],
                            "method": "max_memory_allocated - base over fwd+grad, min of 3 (as the reference)"}
+        peak_fc, ms_fc = stacked_depth(8, dev, module="SwiGLUMLPFullCheckpoint")
+        line["stacked_full_checkpoint"] = {"n_blocks": 8, "peak_mib": round(peak_fc, 1),
+                                           "ms_per_step": round(ms_fc, 3)}
     if not args.no_cpu_baseline:
         tf, cores, sample = cpu_reference_sample(seconds=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",

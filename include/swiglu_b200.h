@@ -74,7 +74,9 @@ int swiglu_b200_device_status(uint32_t* bits, int clear);
 int swiglu_b200_set_gemm_path(int mode);
 
 /* One launch: preact [M, 2H] = x [M, K] . W1^T and h [M, H] = left * silu(gate).
- * h may be NULL (preact only).
+ * h may be NULL (preact only); preact may be NULL (h only: the no-save
+ * inference forward, the external `fused_swiglu_wide_packed` that
+ * bench_packed_vs_cublas.py:25-30,72 measures).
  *   w_form = T, layout = STD:       fused_matmul_swiglu_save_preact   fused_forward.py:188-256
  *   w_form = T, layout = PACKED128: fused_swiglu_save_preact_packed    fused_forward_packed.py:186-216
  *                                   (and fused_forward_packed_canon.py:103-134)

@@ -334,7 +334,7 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   if (K <= 0 || H <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K and H must be positive");
   if (group_m < 1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "group_size_m must be >= 1");
   if (M == 0) return SWIGLU_OK;
-  if (!x || !w || !preact) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!x || !w || (!preact && !h)) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
   DeviceInfo* d;
   if (int rc = current_device(&d)) return rc;
   if (dtype == SWIGLU_F32) {
@@ -369,7 +369,7 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   p.tiles_n = (int)((H + 127) / 128);
   p.group_m = group_m;
   p.flags = rounded ? kFlagHFromRounded : 0;
-  if (reinterpret_cast<uintptr_t>(preact) % 16 || (h && reinterpret_cast<uintptr_t>(h) % 16))
+  if ((preact && reinterpret_cast<uintptr_t>(preact) % 16) || (h && reinterpret_cast<uintptr_t>(h) % 16))
     return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
   return w_form == SWIGLU_W1_ROWS ? run_gemm<false, false, kEpiSwiglu, false>(p, *d, st)
                                   : run_gemm<false, true, kEpiSwiglu, false>(p, *d, st);

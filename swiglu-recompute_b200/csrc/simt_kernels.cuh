@@ -117,8 +117,10 @@ __global__ void __launch_bounds__(256) simt_gemm_f32_kernel(const SimtParams p) 
         const int hj = nt * 32 + cols[j];
         if (hj >= p.N) continue;
         const float l = acc[i][j], g = acc[i][j + 2];
-        p.out0[(long long)r * p.ld0 + left_col(hj, p.H, p.layout)] = l;
-        p.out0[(long long)r * p.ld0 + gate_col(hj, p.H, p.layout)] = g;
+        if (p.out0) {
+          p.out0[(long long)r * p.ld0 + left_col(hj, p.H, p.layout)] = l;
+          p.out0[(long long)r * p.ld0 + gate_col(hj, p.H, p.layout)] = g;
+        }
         if (p.out1) p.out1[(long long)r * p.ld1 + hj] = l * (g * (1.0f / (1.0f + expf(-g))));
       }
     } else {  // kEpiDswiglu: acc = grad_h, preact updated in place

@@ -189,8 +189,10 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
         hf[i] = l * (g * sigmoid_fast(g));
       }
       if (row_ok) {
-        store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
-        store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
+        if (p.out0) {  // preact is not stored by the no-save (inference) forward
+          store_row32<false>(pre_row, left_col(j, p.H, p.layout), left_col(j, p.H, p.layout) + (p.N - j), lf);
+          store_row32<false>(pre_row, gate_col(j, p.H, p.layout), gate_col(j, p.H, p.layout) + (p.N - j), gf);
+        }
         if (h_row) store_row32<false>(h_row, j, p.N, hf);
       }
     }

@@ -108,6 +108,10 @@ class SwiGLUFusedForwardFunction(torch.autograd.Function):
         if not wt.is_contiguous():
             wt = wt.contiguous()
         w2 = w2.contiguous()
+        if not any(ctx.needs_input_grad[:3]):                # inference: h only
+            _, h = ops.swiglu_fwd(x, wt, w_form=W1_T, layout=LAYOUT_STD, h_from_rounded=False,
+                                  want_preact=False)
+            return ops.matmul(h, w2, a_t=False, b_t=True)
         preact, h = fused_matmul_swiglu_save_preact(x, wt)   # one kernel
         ctx.save_for_backward(x, wt, w2, preact)             # save preact, NOT h
         y = ops.matmul(h, w2, a_t=False, b_t=True)           # [M, Dout]

@@ -146,6 +146,19 @@ def fused_swiglu_save_preact_packed(x, packed_weight):
     return h, preact
 
 
+def fused_swiglu_packed_no_save(x, packed_weight):
+    """h [M, H] only: the no-save (inference) packed forward, the kernel the
+    reference measures from outside its tree (bench_packed_vs_cublas.py:25-30,72)."""
+    assert x.is_cuda and packed_weight.is_cuda
+    assert x.is_contiguous() and packed_weight.is_contiguous()
+    m, k = x.shape
+    k2, n2 = packed_weight.shape
+    assert k == k2 and n2 % 2 == 0 and (n2 // 2) % BLOCK_SIZE_N_HALF == 0
+    _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128, h_from_rounded=False,
+                          want_preact=False, group_size_m=GROUP_SIZE_M)
+    return h
+
+
 # -----------------------------------------------------------------------------
 # Backward pointwise: packed grad_de from packed preact + dy (fresh output)
 # (fused_forward_packed.py:262-277)
@@ -180,6 +193,10 @@ class SwiGLUPackedFusedFunction(torch.autograd.Function):
         if not packed_weight.is_contiguous():
             packed_weight = packed_weight.contiguous()
         w2 = w2.contiguous()
+        if not any(ctx.needs_input_grad[:3]):                          # inference: h only
+            _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
+                                  h_from_rounded=False, want_preact=False, group_size_m=GROUP_SIZE_M)
+            return ops.matmul(h, w2, a_t=False, b_t=True)
         h, preact = fused_swiglu_save_preact_packed(x, packed_weight)  # one kernel
         ctx.save_for_backward(x, packed_weight, w2, preact)            # save preact, NOT h
         y = ops.matmul(h, w2, a_t=False, b_t=True)

@@ -60,6 +60,10 @@ class SwiGLUPackedFusedFunctionCanon(torch.autograd.Function):
         if not packed_weight.is_contiguous():
             packed_weight = packed_weight.contiguous()
         w2 = w2.contiguous()
+        if not any(ctx.needs_input_grad[:3]):                          # inference: h only
+            _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
+                                  h_from_rounded=False, want_preact=False, group_size_m=GROUP_SIZE_M)
+            return ops.matmul(h, w2, a_t=False, b_t=True)
         h, preact = fused_swiglu_save_preact_packed_canon(x, packed_weight)
         ctx.save_for_backward(x, packed_weight, w2, preact)
         return ops.matmul(h, w2, a_t=False, b_t=True)

@@ -63,9 +63,11 @@ def _same_dtype(*ts: torch.Tensor) -> torch.dtype:
 
 
 def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
-               h_from_rounded: bool, want_h: bool = True,
+               h_from_rounded: bool, want_h: bool = True, want_preact: bool = True,
                group_size_m: int = DEFAULT_GROUP_M):
-    """(preact [M, 2H], h [M, H] or None) for preact = x . W1^T in one launch."""
+    """(preact [M, 2H] or None, h [M, H] or None) for preact = x . W1^T in one
+    launch. want_preact=False is the no-save (inference) forward."""
+    assert want_h or want_preact
     dev = _check_cuda(x, w)
     dt = _same_dtype(x, w)
     M, K = x.shape
@@ -75,7 +77,7 @@ def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
         K2, n2 = w.shape
     assert K == K2 and n2 % 2 == 0, f"shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}"
     H = n2 // 2
-    preact = torch.empty((M, n2), device=dev, dtype=dt)
+    preact = torch.empty((M, n2), device=dev, dtype=dt) if want_preact else None
     h = torch.empty((M, H), device=dev, dtype=dt) if want_h else None
     with torch.cuda.device(dev):
         _lib.call("swiglu_b200_fused_matmul_swiglu_save_preact", _p(x), _p(w), _p(preact), _p(h),

@@ -101,11 +101,15 @@ class SwiGLUMemoryOptimizedFunction(torch.autograd.Function):
         lead = x.shape[:-1]
         x2 = _flatten_rows(x)
         W1c, W2c = W1.contiguous(), W2.contiguous()
-        # preact [M, 2H] and the transient h [M, H] from one tcgen05 launch.
-        preact, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+        training = any(ctx.needs_input_grad[:3])
+        # preact [M, 2H] and the transient h [M, H] from one tcgen05 launch;
+        # with no gradient needed, the no-save forward writes h only.
+        preact, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
+                                   want_preact=training)
         y = ops.matmul(h, W2c, a_t=False, b_t=True)            # [M, Dout] = h W2^T
         del h                                                 # h is NOT retained
-        ctx.save_for_backward(x2, W1c, W2c, preact)
+        if training:
+            ctx.save_for_backward(x2, W1c, W2c, preact)
         ctx.x_shape = x.shape
         return y.reshape(*lead, W2.shape[0])
 
@@ -114,6 +118,43 @@ class SwiGLUMemoryOptimizedFunction(torch.autograd.Function):
         x, W1, W2, preact = ctx.saved_tensors
         gx, gw1, gw2 = _recompute_backward(ctx, grad_y, x, W1, W2, preact,
                                            w_form=W1_ROWS, layout=LAYOUT_STD)
+        if gx is not None:
+            gx = gx.reshape(ctx.x_shape)
+        return gx, gw1, gw2
+
+
+class SwiGLUFullCheckpointFunction(torch.autograd.Function):
+    """Full-checkpoint variant: saves only x (and the weights), not preact.
+
+    The backward recomputes preact with the GEMM1 kernel (preact only, no h)
+    and then runs the same backward as SwiGLUMemoryOptimizedFunction, so its
+    results are bit-identical to it. Per block it saves [M, D] instead of
+    [M, D] + [M, 2H], for one extra GEMM1 (2*M*D*2H FLOPs) in backward: the
+    next memory lever named in the reference's analysis
+    (training_memory_forward_vs_backward.md:217-221). No counterpart module
+    exists in the reference.
+    """
+
+    @staticmethod
+    def forward(ctx, x, W1, W2):
+        lead = x.shape[:-1]
+        x2 = _flatten_rows(x)
+        W1c, W2c = W1.contiguous(), W2.contiguous()
+        _, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
+                              want_preact=False)
+        y = ops.matmul(h, W2c, a_t=False, b_t=True)
+        del h
+        if any(ctx.needs_input_grad[:3]):
+            ctx.save_for_backward(x2, W1c, W2c)
+        ctx.x_shape = x.shape
+        return y.reshape(*lead, W2.shape[0])
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        x, W1, W2 = ctx.saved_tensors
+        preact, _ = ops.swiglu_fwd(x, W1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
+                                   want_h=False)
+        gx, gw1, gw2 = _recompute_backward(ctx, grad_y, x, W1, W2, preact, w_form=W1_ROWS, layout=LAYOUT_STD)
         if gx is not None:
             gx = gx.reshape(ctx.x_shape)
         return gx, gw1, gw2
@@ -137,6 +178,13 @@ class SwiGLUMLPCustom(nn.Module):
 
     def forward(self, x):
         return SwiGLUMemoryOptimizedFunction.apply(x, self.w1, self.w2)
+
+
+class SwiGLUMLPFullCheckpoint(SwiGLUMLPCustom):
+    """SwiGLUMLPCustom with full checkpointing: saves only x, recomputes preact."""
+
+    def forward(self, x):
+        return SwiGLUFullCheckpointFunction.apply(x, self.w1, self.w2)
 
 
 class SwiGLUMLPGroundTruth(nn.Module):
