@@ -19,6 +19,7 @@
 #ifndef SWIGLU_B200_H
 #define SWIGLU_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -72,6 +73,23 @@ int swiglu_b200_device_status(uint32_t* bits, int clear);
  * and tuning. No reference counterpart (the reference's Triton kernels pick
  * their tiling at compile time, fused_forward.py:55-65). */
 int swiglu_b200_set_gemm_path(int mode);
+
+/* Recommended size of a stream-K workspace (48 MiB). */
+#define SWIGLU_B200_STREAM_WORKSPACE_BYTES ((size_t)48 << 20)
+
+/* Registers `workspace` (device memory of the current device, 256-byte
+ * aligned, `bytes` >= 4096, the first 4096 bytes zero-filled) for GEMMs
+ * launched on `stream`; NULL unregisters. With a workspace, the 2-SM GEMM
+ * kernels split the tiles of their last, partial round of CTA pairs along K
+ * (stream-K), so every pair stays busy to the end; the parts are added in a
+ * fixed order, so results are run-to-run identical, but differ from the
+ * unsplit kernel in f32 summation order. Without one (or one too small for a
+ * launch) the unsplit kernel runs. Launches on one stream share its
+ * workspace in stream order and leave its first 4096 bytes zero; the buffer
+ * must stay allocated while registered. Plays the part of the scratch
+ * allocator the reference installs for its Triton kernels
+ * (fused_forward.py:68-74, triton.set_allocator). */
+int swiglu_b200_set_stream_workspace(void* workspace, size_t bytes, void* stream);
 
 /* One launch: preact [M, 2H] = x [M, K] . W1^T and h [M, H] = left * silu(gate).
  * h may be NULL (preact only); preact may be NULL (h only: the no-save

@@ -1,6 +1,6 @@
 // Host side of the C ABI declared in include/swiglu_b200.h: argument checks,
 // TMA tensor-map encoding, kernel selection and launch. No allocation: every
-// buffer is the caller's.
+// buffer, including the per-stream stream-K workspace, is the caller's.
 #include "swiglu_b200.h"
 
 #include <cuda_runtime.h>
@@ -208,16 +208,8 @@ int launch_single(const Params& p, int tiles, int threads, int smem, const Devic
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, what);
 }
 
-// Persistent CTA-pair launch (clusters of 2): as many pairs as fit at once,
-// at most one per tile.
-template <auto kern, class Params>
-int launch_pair(const Params& p, int tiles, int threads, int smem, const DeviceInfo& d, cudaStream_t st,
-                const char* what) {
-  KernelState& ks = kernel_state<kern>();
-  int dev = 0;
-  cudaGetDevice(&dev);
+cudaLaunchConfig_t pair_launch_config(cudaLaunchAttribute* attr, int threads, int smem, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -227,9 +219,21 @@ int launch_pair(const Params& p, int tiles, int threads, int smem, const DeviceI
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cfg;
+}
+
+// How many CTA pairs of `kern` fit on the current device at once (queried
+// once per device).
+template <auto kern>
+int pair_capacity(int threads, int smem, const DeviceInfo& d, int* out, const char* what) {
+  KernelState& ks = kernel_state<kern>();
+  int dev = 0;
+  cudaGetDevice(&dev);
   if (!(ks.ready.load() & (1ull << dev))) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, what);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pair_launch_config(attr, threads, smem, nullptr);
     cfg.gridDim = dim3(2 * (d.sms / 2));
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
@@ -238,10 +242,125 @@ int launch_pair(const Params& p, int tiles, int threads, int smem, const DeviceI
     ks.max_clusters[dev] = n;
     ks.ready.fetch_or(1ull << dev);
   }
-  const int clusters = tiles < ks.max_clusters[dev] ? tiles : ks.max_clusters[dev];
-  cfg.gridDim = dim3(2 * clusters);
+  *out = ks.max_clusters[dev];
+  return SWIGLU_OK;
+}
+
+// Persistent CTA-pair launch (clusters of 2): as many pairs as fit at once,
+// at most one per work unit.
+template <auto kern, class Params>
+int launch_pair(const Params& p, int units, int threads, int smem, const DeviceInfo& d, cudaStream_t st,
+                const char* what) {
+  int cap = 0;
+  if (int rc = pair_capacity<kern>(threads, smem, d, &cap, what)) return rc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_launch_config(attr, threads, smem, st);
+  cfg.gridDim = dim3(2 * (units < cap ? units : cap));
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, what);
+}
+
+// ------------------------------------------------------------ stream-K workspaces
+// A caller-owned device buffer per (device, stream), registered with
+// swiglu_b200_set_stream_workspace. Layout: kSkCounterBytes of arrival
+// counters (zero when registered; every launch leaves them zero), then the
+// f32 partial tiles.
+constexpr size_t kSkCounterBytes = 4096;
+constexpr int kSkMaxSplit = 4;      // at most 4 parts per tail tile
+constexpr int kSkMinBlocksPerPart = 4;
+
+struct StreamWorkspace {
+  int dev = -1;
+  cudaStream_t stream = nullptr;
+  uint8_t* ptr = nullptr;
+  size_t bytes = 0;
+  uint32_t epoch = 0;
+};
+constexpr int kMaxWorkspaces = 256;
+std::mutex g_ws_mu;
+StreamWorkspace g_ws[kMaxWorkspaces];
+
+int set_workspace(void* ptr, size_t bytes, cudaStream_t st) {
+  int dev = 0;
+  if (int rc = resolve_device(&dev)) return rc;
+  if (ptr && (reinterpret_cast<uintptr_t>(ptr) % 256))
+    return fail(SWIGLU_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  if (ptr && bytes < kSkCounterBytes)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is below the %zu-byte minimum", bytes,
+                kSkCounterBytes);
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  StreamWorkspace* slot = nullptr;
+  for (auto& w : g_ws) {
+    if (w.ptr && w.dev == dev && w.stream == st) slot = &w;
+  }
+  if (!ptr) {
+    if (slot) *slot = StreamWorkspace{};
+    return SWIGLU_OK;
+  }
+  if (!slot) {
+    for (auto& w : g_ws) {
+      if (!w.ptr) {
+        slot = &w;
+        break;
+      }
+    }
+  }
+  if (!slot) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "more than %d stream workspaces registered", kMaxWorkspaces);
+  *slot = StreamWorkspace{dev, st, static_cast<uint8_t*>(ptr), bytes, slot->epoch};
+  return SWIGLU_OK;
+}
+
+// The workspace of (current device, st) and a fresh epoch for one launch;
+// false when none is registered.
+bool take_workspace(cudaStream_t st, uint8_t** ptr, size_t* bytes, uint32_t* epoch) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  for (auto& w : g_ws) {
+    if (w.ptr && w.dev == dev && w.stream == st) {
+      w.epoch = w.epoch % 0xFFFFFFu + 1u;
+      *ptr = w.ptr;
+      *bytes = w.bytes;
+      *epoch = w.epoch;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Chooses the stream-K tail of a persistent launch of `tiles` tiles of
+// `tile_floats` f32 accumulators on `clusters` pairs with `num_kb` K blocks:
+// the tiles of the last, partial round are split into as many K ranges as
+// there are idle pairs for (at most kSkMaxSplit, each of at least
+// kSkMinBlocksPerPart blocks), if the stream has a workspace large enough.
+// `slabs` arrival counters are used per tail tile.
+void choose_stream_k(int tiles, int clusters, int num_kb, long long tile_floats, int slabs, cudaStream_t st,
+                     float** partials, uint32_t** counters, int* tail_out, int* split_out, uint32_t* epoch_out) {
+  *tail_out = 0;
+  *split_out = 1;
+  const int tail = tiles % clusters;
+  if (tail == 0) return;
+  // Only where the idle pairs of the last round are at least 5% of the
+  // launch's pair-rounds: below that, the partial-tile traffic and the longer
+  // epilogue of the finishing part cost about what the split wins (measured
+  // at M=11136 on the grad_h GEMM: 2464 tiles, 2% idle, 2% slower split).
+  const int rounds = (tiles + clusters - 1) / clusters;
+  if ((clusters - tail) * 20 < clusters * rounds) return;
+  int split = clusters / tail;
+  if (split > kSkMaxSplit) split = kSkMaxSplit;
+  if (split > num_kb / kSkMinBlocksPerPart) split = num_kb / kSkMinBlocksPerPart;
+  if (split < 2) return;
+  uint8_t* ws = nullptr;
+  size_t bytes = 0;
+  uint32_t epoch = 0;
+  if (static_cast<size_t>(tail) * slabs * 4 > kSkCounterBytes) return;
+  const size_t need = kSkCounterBytes + static_cast<size_t>(tail) * split * tile_floats * 4;
+  if (!take_workspace(st, &ws, &bytes, &epoch) || bytes < need) return;
+  *counters = reinterpret_cast<uint32_t*>(ws);
+  *partials = reinterpret_cast<float*>(ws + kSkCounterBytes);
+  *tail_out = tail;
+  *split_out = split;
+  *epoch_out = epoch;
 }
 
 template <class Cfg>
@@ -255,11 +374,18 @@ int launch_tc(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
 
 template <class Cfg>
 int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+  constexpr auto kern = tc_gemm2_kernel<Cfg>;
+  const char* what = "2-SM tcgen05 GEMM launch";
   p.mn_lbo = kMnLbo;
   p.mn_sbo = kMnSbo;
   p.status = d.status;
-  return launch_pair<tc_gemm2_kernel<Cfg>>(p, p.tiles_m * p.tiles_n, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, st,
-                     "2-SM tcgen05 GEMM launch");
+  int cap = 0;
+  if (int rc = pair_capacity<kern>(Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, &cap, what)) return rc;
+  const int tiles = p.tiles_m * p.tiles_n;
+  // 8 slabs of 32 rows per 256-row tile: 4 epilogue warps in each CTA.
+  choose_stream_k(tiles, cap, (p.K + Cfg::BK - 1) / Cfg::BK, static_cast<long long>(Cfg::BM) * Cfg::BN, 8, st,
+                  &p.sk_partials, &p.sk_counters, &p.sk_tail, &p.sk_split, &p.sk_epoch);
+  return launch_pair<kern>(p, tiles + p.sk_tail * (p.sk_split - 1), Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, st, what);
 }
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
@@ -580,8 +706,17 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   if (mode == 0) mode = pair_tiles >= d->sms / 2 ? 2 : 1;
   if (mode == 2) {
     p.tiles_j = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ);
-    return launch_pair<dw2_hprologue_pair_kernel>(p, pair_tiles, Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES,
-                       *d, st, "dW2 (CTA pair)");
+    const char* what = "dW2 (CTA pair)";
+    int cap = 0;
+    if (int rc = pair_capacity<dw2_hprologue_pair_kernel>(Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES, *d, &cap,
+                                                         what))
+      return rc;
+    // 8 slabs of 32 hidden units per 256-unit tile: 4 epilogue warps per CTA.
+    choose_stream_k(pair_tiles, cap, (int)((M + Dw2PairCfg::BK - 1) / Dw2PairCfg::BK),
+                    static_cast<long long>(Dw2PairCfg::BJ) * Dw2PairCfg::BD, 8, st, &p.sk_partials, &p.sk_counters,
+                    &p.sk_tail, &p.sk_split, &p.sk_epoch);
+    return launch_pair<dw2_hprologue_pair_kernel>(p, pair_tiles + p.sk_tail * (p.sk_split - 1),
+                                                  Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES, *d, st, what);
   }
   p.tiles_j = (int)((H + Dw2Cfg::BJ - 1) / Dw2Cfg::BJ);
   return launch_single<dw2_hprologue_kernel>(p, p.tiles_j * p.tiles_d, Dw2Cfg::NUM_THREADS, Dw2Cfg::SMEM_BYTES,
@@ -806,6 +941,10 @@ int swiglu_b200_matmul_reduce_rows_noalloc(const void* a, const void* b, void* o
                                            int64_t K, int a_layout, int b_layout, int out_dtype, void* stream) {
   return op_matmul_reduce_noalloc(a, b, out, M, N, K, a_layout, b_layout, out_dtype,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_set_stream_workspace(void* workspace, size_t bytes, void* stream) {
+  return set_workspace(workspace, bytes, static_cast<cudaStream_t>(stream));
 }
 
 int swiglu_b200_set_gemm_path(int mode) {

@@ -29,6 +29,11 @@ struct Dw2Params {
   int layout;
   int tiles_j, tiles_d;  // hidden blocks of 128, output blocks of 512
   uint32_t* status;
+  // Stream-K tail of the pair kernel, as in TcParams (partials [tail][split][256][512]).
+  float* sk_partials;
+  uint32_t* sk_counters;
+  int sk_tail, sk_split;
+  uint32_t sk_epoch;
 };
 
 struct Dw2Cfg {
@@ -339,9 +344,10 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = p.tiles_j * p.tiles_d;
+  const int num_units = sk_units(num_tiles, p.sk_tail, p.sk_split);
   const int num_kb = (p.M + BK - 1) / BK;
-  const int first_tile = static_cast<int>(cluster_id_x());
-  const int tile_step = static_cast<int>(num_clusters_x());
+  const int first_unit = static_cast<int>(cluster_id_x());
+  const int unit_step = static_cast<int>(num_clusters_x());
   uint32_t* status = p.status;
   auto tile_jd = [&](int tile, int& tj, int& td) {
     tj = tile / p.tiles_d;
@@ -354,14 +360,15 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
       tma_prefetch_desc(&p.tm_gy);
       uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      for (int u = first_unit; u < num_units && ok; u += unit_step) {
+        const SkUnit w = sk_unit_of(num_tiles, p.sk_tail, p.sk_split, u, num_kb);
         int tj, td;
-        tile_jd(tile, tj, td);
+        tile_jd(w.tile, tj, td);
         const int j0 = tj * C::BJ + C::BJH * static_cast<int>(rank);
         const int lc = left_col(j0, p.H, p.layout);
         const int gc = gate_col(j0, p.H, p.layout);
         const int d0 = td * C::BD + 128 * static_cast<int>(rank);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -401,10 +408,11 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
       constexpr uint32_t idesc = make_idesc_f16(256, 256, 1, 1, 1, 1);
       uint32_t stage = 0, phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      for (int u = first_unit; u < num_units && ok; u += unit_step) {
+        const SkUnit w = sk_unit_of(num_tiles, p.sk_tail, p.sk_split, u, num_kb);
         if (!mbar_wait(tmem_empty, acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
         tc_fence_after_sync();
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&b_full[stage], phase, abort_flag, status, kErrTimeoutMma) ||
               !mbar_wait(&ready[stage], phase, abort_flag, status, kErrTimeoutMma)) {
             ok = false;
@@ -418,7 +426,7 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
             const uint64_t adesc = make_smem_desc_sw128(sa + k * 2048, C::BOX_BYTES, 1024);
             const uint64_t b0 = make_smem_desc_sw128(sb + k * 2048, C::BOX_BYTES, 1024);
             const uint64_t b1 = make_smem_desc_sw128(sb + 2 * C::BOX_BYTES + k * 2048, C::BOX_BYTES, 1024);
-            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            const uint32_t acc = (kb != w.kb0 || k != 0) ? 1u : 0u;
             umma_f16_ss_pair(tmem_base, adesc, b0, idesc, acc);
             umma_f16_ss_pair(tmem_base + 256, adesc, b1, idesc, acc);
           }
@@ -441,17 +449,29 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
   } else if (warp < 6) {
     const uint32_t q = warp & 3u;
     uint32_t acc_phase = 0;
-    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+    for (int u = first_unit; u < num_units; u += unit_step) {
+      const SkUnit w = sk_unit_of(num_tiles, p.sk_tail, p.sk_split, u, num_kb);
       int tj, td;
-      tile_jd(tile, tj, td);
+      tile_jd(w.tile, tj, td);
       if (!mbar_wait(tmem_full, acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
       tc_fence_after_sync();
-      const int j = tj * C::BJ + C::BJH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const int j_in_tile = C::BJH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const int j = tj * C::BJ + j_in_tile;
       const bool j_ok = j < p.H;
       const int d0 = td * C::BD;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16);
+      bool finish = true;
+      if (w.parts > 1) {
+        // Stream-K part: the last of the parts to arrive for this 32-row
+        // slab finishes the tile.
+        const int i = w.tile - (num_tiles - p.sk_tail);
+        const long long part_stride = static_cast<long long>(C::BJ) * C::BD;
+        const float* fix = p.sk_partials + (static_cast<long long>(i) * w.parts * C::BJ + j_in_tile) * C::BD;
+        finish = sk_publish_and_fix(t_row, C::BD, const_cast<float*>(fix) + w.part * part_stride, fix, part_stride,
+                                    w.parts, p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch);
+      }
 #pragma unroll 1
-      for (int c = 0; c < C::BD / 32; ++c) {
+      for (int c = 0; c < (finish ? C::BD / 32 : 0); ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
@@ -482,8 +502,9 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
     constexpr int kChunks = C::A_BYTES / 16;
     uint32_t stage = 0, phase = 0;
     bool ok = true;
-    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
-      for (int kb = 0; kb < num_kb; ++kb) {
+    for (int u = first_unit; u < num_units && ok; u += unit_step) {
+      const SkUnit w = sk_unit_of(num_tiles, p.sk_tail, p.sk_split, u, num_kb);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (stage % C::XFORM_GROUPS == grp) {
           if (!mbar_wait(&lg_full[stage], phase, abort_flag, status, kErrTimeoutTransform)) {
             ok = false;

@@ -68,7 +68,112 @@ struct TcParams {
   // (row pitch ld0). The buffers may be other GPUs' memory (NVLink P2P).
   float* peer[8];
   int rows_per_rank, src_rank;
+  // Stream-K tail (2-SM kernel only). The last `sk_tail` tiles of the tile
+  // order are each computed as `sk_split` parts over equal K ranges by
+  // different CTA pairs, so the last round keeps every pair busy. Each part
+  // leaves its f32 accumulator tile in `sk_partials` ([tail][split][BM][BN]);
+  // per 32-row slab, the warp that arrives last on `sk_counters` (epoch-tagged,
+  // see sk_arrive_last) adds the parts in part order and runs the epilogue.
+  // sk_split <= 1 disables it (sk_tail is then 0).
+  float* sk_partials;
+  uint32_t* sk_counters;
+  int sk_tail, sk_split;
+  uint32_t sk_epoch;  // 1 .. 2^24-1, new for every launch
 };
+
+// One unit of stream-K work: tile `tile`, K blocks [kb0, kb1), part `part` of
+// `parts` (parts == 1: a whole tile).
+struct SkUnit {
+  int tile, part, parts, kb0, kb1;
+};
+
+// Units of a launch of `tiles` tiles whose last `tail` tiles are split into
+// `split` parts. Unit u < tiles - tail is tile u; then come the parts, tile
+// by tile.
+__device__ __forceinline__ int sk_units(int tiles, int tail, int split) { return tiles + tail * (split - 1); }
+
+__device__ __forceinline__ SkUnit sk_unit_of(int tiles, int tail, int split, int u, int num_kb) {
+  const int full = tiles - tail;
+  if (u < full) return {u, 0, 1, 0, num_kb};
+  const int v = u - full, i = v / split, s = v - i * split;
+  return {full + i, s, split, s * num_kb / split, (s + 1) * num_kb / split};
+}
+
+__device__ __forceinline__ int sk_num_units(const TcParams& p) {
+  return sk_units(p.tiles_m * p.tiles_n, p.sk_tail, p.sk_split);
+}
+
+__device__ __forceinline__ SkUnit sk_unit(const TcParams& p, int u, int num_kb) {
+  return sk_unit_of(p.tiles_m * p.tiles_n, p.sk_tail, p.sk_split, u, num_kb);
+}
+
+// Counts one arrival of `parts` on an epoch-tagged counter (epoch in the high
+// 24 bits, arrivals in the low 8). A counter holding another epoch (zero, or a
+// launch that stopped early) counts as empty. The last arrival resets it to
+// zero. Returns true for the last arrival. Called by one lane.
+__device__ __forceinline__ bool sk_arrive_last(uint32_t* ctr, uint32_t epoch, int parts) {
+  const uint32_t tag = epoch << 8;
+  uint32_t cur = *reinterpret_cast<volatile uint32_t*>(ctr), seen, next;
+  do {
+    seen = cur;
+    next = ((seen & 0xFFFFFF00u) == tag ? seen : tag) + 1u;
+    cur = atomicCAS(ctr, seen, next);
+  } while (cur != seen);
+  const bool last = static_cast<int>(next & 0xFFu) == parts;
+  if (last) atomicExch(ctr, 0u);
+  return last;
+}
+
+// Stream-K part of one epilogue warp (32 accumulator rows of `ncols` f32
+// columns at TMEM address `t_row`): publishes this part's rows at `mine`,
+// counts the arrival, and returns true if this warp arrived last for its
+// slab; it then holds the sum of all parts (`fix` = the row in part 0, parts
+// `part_stride` floats apart, added in part order so the result does not
+// depend on which part finished last) in TMEM in place of its own part, and
+// the ordinary epilogue can run.
+__device__ __noinline__ bool sk_publish_and_fix(uint32_t t_row, int ncols, float* mine, const float* fix,
+                                                long long part_stride, int parts, uint32_t* counter, uint32_t epoch) {
+#pragma unroll 1
+  for (int c = 0; c < ncols; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+    float4* dst = reinterpret_cast<float4*>(mine + c);
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      __stcg(dst + g, make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                  __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+  }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if ((threadIdx.x & 31) == 0) last = sk_arrive_last(counter, epoch, parts);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return false;
+  __threadfence();
+#pragma unroll 1
+  for (int c = 0; c < ncols; c += 32) {
+    float acc[32];
+#pragma unroll 1
+    for (int s = 0; s < parts; ++s) {
+      const float4* f = reinterpret_cast<const float4*>(fix + s * part_stride + c);
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const float4 v = __ldcg(f + g);
+        acc[4 * g + 0] = s ? acc[4 * g + 0] + v.x : v.x;
+        acc[4 * g + 1] = s ? acc[4 * g + 1] + v.y : v.y;
+        acc[4 * g + 2] = s ? acc[4 * g + 2] + v.z : v.z;
+        acc[4 * g + 3] = s ? acc[4 * g + 3] + v.w : v.w;
+      }
+    }
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(acc[i]);
+    tmem_st_32x32b_x32(t_row + c, r);
+  }
+  tmem_st_wait();
+  return true;
+}
 
 // Shared-memory staging per epilogue warp for kEpiScatterRows: a 32 x 32 f32
 // block with a 33-float row pitch (bank-conflict-free both ways).

@@ -87,10 +87,10 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int num_units = sk_num_units(p);
   const int num_kb = (p.K + BK - 1) / BK;
-  const int first_tile = static_cast<int>(cluster_id_x());
-  const int tile_step = static_cast<int>(num_clusters_x());
+  const int first_unit = static_cast<int>(cluster_id_x());
+  const int unit_step = static_cast<int>(num_clusters_x());
   uint32_t* status = p.status;
 
   if (warp == 0) {
@@ -99,9 +99,10 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       tma_prefetch_desc(&p.tmB);
       uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      for (int u = first_unit; u < num_units && ok; u += unit_step) {
+        const SkUnit w = sk_unit(p, u, num_kb);
         int pm, pn;
-        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
         const int m0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank);
         int b0;  // first column of this CTA's half of B
         if constexpr (Cfg::EPI == kEpiSwiglu) {
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         } else {
           b0 = pn * BN + (BN / 2) * static_cast<int>(rank);
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -153,11 +154,12 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       constexpr uint32_t idesc = make_idesc_f16(256, BN, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      for (int u = first_unit; u < num_units && ok; u += unit_step) {
+        const SkUnit w = sk_unit(p, u, num_kb);
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -171,7 +173,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
                                              : make_smem_desc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sb + k * 2048, p.mn_lbo, p.mn_sbo)
                                              : make_smem_desc_sw128(sb + k * 32, 16, 1024);
-            umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(map_to_rank(&empty[stage], 0));
           umma_commit_pair(map_to_rank(&empty[stage], 1));
@@ -195,16 +197,29 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
   } else {
     const uint32_t q = warp & 3u;
     uint32_t acc = 0, acc_phase = 0;
-    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+    for (int u = first_unit; u < num_units; u += unit_step) {
+      const SkUnit w = sk_unit(p, u, num_kb);
       int pm, pn;
-      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
       if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
       tc_fence_after_sync();
-      const int row = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const int row_in_tile = Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
+      const int row = pm * Cfg::BM + row_in_tile;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
       float* stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES) +
                      (warp - 2) * kScatterStageFloats;
-      epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+      if (w.parts == 1) {
+        epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+      } else {
+        // Stream-K part: the last of the parts to arrive for this 32-row
+        // slab finishes the tile.
+        const int i = w.tile - (p.tiles_m * p.tiles_n - p.sk_tail);
+        const long long part_stride = static_cast<long long>(Cfg::BM) * BN;
+        const float* fix = p.sk_partials + (static_cast<long long>(i) * w.parts * Cfg::BM + row_in_tile) * BN;
+        if (sk_publish_and_fix(t_row, BN, const_cast<float*>(fix) + w.part * part_stride, fix, part_stride, w.parts,
+                               p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch))
+          epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+      }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[acc], 0));

@@ -30,6 +30,7 @@ _SIGNATURES = {
     "swiglu_b200_last_error_message": [],
     "swiglu_b200_device_status": [ctypes.POINTER(ctypes.c_uint32), _i],
     "swiglu_b200_set_gemm_path": [_i],
+    "swiglu_b200_set_stream_workspace": [_p, ctypes.c_size_t, _p],
     "swiglu_b200_fused_matmul_swiglu_save_preact":
         [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
     "swiglu_b200_matmul": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],

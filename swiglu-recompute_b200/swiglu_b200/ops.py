@@ -30,8 +30,40 @@ def _p(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
+# Stream-K workspace per (device index, stream handle): registered with the
+# library the first time a stream is used, zero-filled by a memset ordered on
+# that stream, and kept for the life of the process.
+STREAM_WORKSPACE_BYTES = 48 << 20
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_stream_k = True
+
+
 def _stream(dev: torch.device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    """Handle of `dev`'s current torch stream (the caller has made `dev`
+    current), with its stream-K workspace registered."""
+    s = torch.cuda.current_stream(dev).cuda_stream
+    key = (dev.index, s)
+    # No registration inside a graph capture: the buffer would belong to the
+    # graph's private memory pool.
+    if _stream_k and key not in _workspaces and not torch.cuda.is_current_stream_capturing():
+        buf = torch.zeros(STREAM_WORKSPACE_BYTES, dtype=torch.uint8, device=dev)
+        _lib.call("swiglu_b200_set_stream_workspace", _p(buf), buf.numel(), ctypes.c_void_p(s))
+        _workspaces[key] = buf
+    return ctypes.c_void_p(s)
+
+
+def set_stream_k(enabled: bool) -> None:
+    """Enables (default) or disables the stream-K tail of the 2-SM GEMMs for
+    later calls. Disabling unregisters every workspace this module registered;
+    the kernels then run unsplit (results differ in f32 summation order)."""
+    global _stream_k
+    _stream_k = bool(enabled)
+    if not enabled:
+        for (index, s) in list(_workspaces):
+            with torch.cuda.device(index):
+                _lib.call("swiglu_b200_set_stream_workspace", None, 0, ctypes.c_void_p(s))
+                torch.cuda.synchronize()
+        _workspaces.clear()
 
 
 def _check_cuda(*ts: torch.Tensor) -> torch.device:
