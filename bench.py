@@ -174,7 +174,7 @@ def kernel_breakdown(x, w1, w2, gy, iters):
     from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
 
     st = torch.cuda.current_stream()
-    names = ["gemm1_swiglu", "gemm2_y", "dw2_hprologue", "gradh_dswiglu_inplace", "dw1", "dx"]
+    names = ["gemm1_swiglu", "gemm2_y", "gradh_dswiglu_emit_h", "dw2_gemm", "dw1", "dx"]
     evs = []
     for _ in range(iters):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
@@ -183,11 +183,14 @@ def kernel_breakdown(x, w1, w2, gy, iters):
         ev[1].record(st)
         y = ops.matmul(h, w2, a_t=False, b_t=True)
         ev[2].record(st)
-        del h, y
-        dw2 = ops.bwd_dw2(gy, preact, layout=LAYOUT_STD)
+        del y
+        # the backward's order (swiglu_recompute._recompute_backward): grad_h
+        # GEMM writing grad_preact in place and h, then dW2 = grad_y^T h
+        ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD, h_out=h)
         ev[3].record(st)
-        ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD)
+        dw2 = ops.matmul(gy, h, a_t=True, b_t=False)
         ev[4].record(st)
+        del h
         dw1 = ops.matmul(preact, x, a_t=True, b_t=False)
         ev[5].record(st)
         dx = ops.matmul(preact, w1, a_t=False, b_t=False)
@@ -205,8 +208,8 @@ def kernel_breakdown(x, w1, w2, gy, iters):
 def kernel_flops(M, D, H, Dout):
     g1 = 2.0 * M * D * 2 * H
     g2 = 2.0 * M * H * Dout
-    return {"gemm1_swiglu": g1, "gemm2_y": g2, "dw2_hprologue": g2, "gradh_dswiglu_inplace": g2,
-            "dw1": g1, "dx": g1}
+    return {"gemm1_swiglu": g1, "gemm2_y": g2, "gradh_dswiglu_emit_h": g2, "dw2_gemm": g2,
+            "dw2_hprologue": g2, "dw1": g1, "dx": g1}
 
 
 def run_kernel_only(args):
@@ -225,14 +228,16 @@ def run_kernel_only(args):
         "gemm1": lambda: ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True),
         "y": lambda: ops.matmul(h, w2, a_t=False, b_t=True),
         "dw2": lambda: ops.bwd_dw2(gy, preact, layout=LAYOUT_STD),
+        "dw2gemm": lambda: ops.matmul(gy, h, a_t=True, b_t=False),
         # in place on a scratch copy so repeated launches see the same input
-        "gradh": lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD),
+        "gradh": lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD, h_out=h),
         "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False),
         "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False),
     }
     pre2 = torch.empty_like(preact) if k == "gradh" else None
     fl = kernel_flops(M, D, H, Dout)[{"gemm1": "gemm1_swiglu", "y": "gemm2_y", "dw2": "dw2_hprologue",
-                                      "gradh": "gradh_dswiglu_inplace", "dw1": "dw1", "dx": "dx"}[k]]
+                                      "dw2gemm": "dw2_gemm", "gradh": "gradh_dswiglu_emit_h", "dw1": "dw1",
+                                      "dx": "dx"}[k]]
     times = []
     for _ in range(args.iters):
         if pre2 is not None:
@@ -461,7 +466,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-stack", action="store_true", help="skip the 8-block stacked-depth memory run")
-    ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "gradh", "dw1", "dx"],
+    ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "dw2gemm", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2], default=0,

@@ -172,6 +172,17 @@ int swiglu_b200_bwd_dw2(const void* grad_y, const void* preact, void* dw2, int64
 int swiglu_b200_bwd_grad_preact_inplace(const void* grad_y, const void* w2, void* preact, int64_t M, int64_t H,
                                         int64_t Dout, int dtype, int layout, void* stream);
 
+/* As swiglu_b200_bwd_grad_preact_inplace, and the same epilogue also writes
+ * h [M, H] = left * silu(gate) of the preact values it replaces (bit-identical
+ * to the h the dW2 prologue recomputes). dW2 then is a plain GEMM,
+ * swiglu_b200_matmul(grad_y, h, dW2, Dout, H, M, a_layout 1, b_layout 0),
+ * with no exp/reciprocal on its tensor-core path; the cost is the transient
+ * [M, H] buffer, the h the reference itself materialises in backward
+ * (swiglu_recompute.py:71). Replaces swiglu_recompute.py:71,74-75 (packed:
+ * fused_forward_packed.py:310,312-313). */
+int swiglu_b200_bwd_grad_preact_inplace_emit_h(const void* grad_y, const void* w2, void* preact, void* h, int64_t M,
+                                               int64_t H, int64_t Dout, int dtype, int layout, void* stream);
+
 /* h [M, H] = left * silu(gate) from preact [M, 2H].
  * _swiglu_forward_logic (swiglu_recompute.py:26-30); packed: _h_from_packed_preact
  * (fused_forward_packed.py:281-286). H % 8 == 0. */

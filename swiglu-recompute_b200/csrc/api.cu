@@ -723,8 +723,12 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
                        *d, st, "dW2");
 }
 
-int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int64_t H, int64_t Dout, int dtype,
-                   int layout, cudaStream_t st) {
+int op_fwd_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout, cudaStream_t st);
+
+// grad_preact in place of preact; with h non-NULL also h = swiglu(preact) of
+// the values it replaced.
+int op_grad_preact(const void* gy, const void* w2, void* preact, void* h, int64_t M, int64_t H, int64_t Dout,
+                   int dtype, int layout, cudaStream_t st) {
   if (int rc = check_dims("bwd_grad_preact_inplace", M, 2 * H, Dout)) return rc;
   if (int rc = check_dtype(dtype)) return rc;
   if (int rc = check_layout(layout, H)) return rc;
@@ -734,6 +738,9 @@ int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int6
   DeviceInfo* d;
   if (int rc = current_device(&d)) return rc;
   if (dtype == SWIGLU_F32) {
+    if (h) {  // fp32 correctness path: h first, from the preact about to be replaced
+      if (int rc = op_fwd_logic(preact, h, M, H, dtype, layout, st)) return rc;
+    }
     SimtParams p{};
     p.a = static_cast<const float*>(gy);
     p.b = static_cast<const float*>(w2);
@@ -750,8 +757,11 @@ int op_grad_preact(const void* gy, const void* w2, void* preact, int64_t M, int6
   if (int rc = map_kmajor(&p.tmA, gy, M, Dout, Dout, 128, "grad_y")) return rc;
   if (int rc = map_mnmajor(&p.tmB, w2, Dout, H, H, "W2")) return rc;
   if (reinterpret_cast<uintptr_t>(preact) % 16) return fail(SWIGLU_ERR_MISALIGNED, "preact must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(h) % 16) return fail(SWIGLU_ERR_MISALIGNED, "h must be 16-byte aligned");
   p.out0 = preact;
   p.ld0 = 2 * H;
+  p.out1 = h;
+  p.ld1 = H;
   p.M = (int)M, p.N = (int)H, p.K = (int)Dout, p.H = (int)H, p.layout = layout;
   p.tiles_n = (int)((H + 255) / 256);
   p.group_m = 16;
@@ -973,7 +983,13 @@ int swiglu_b200_bwd_dw2(const void* grad_y, const void* preact, void* dw2, int64
 
 int swiglu_b200_bwd_grad_preact_inplace(const void* grad_y, const void* w2, void* preact, int64_t M, int64_t H,
                                         int64_t Dout, int dtype, int layout, void* stream) {
-  return op_grad_preact(grad_y, w2, preact, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
+  return op_grad_preact(grad_y, w2, preact, nullptr, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_bwd_grad_preact_inplace_emit_h(const void* grad_y, const void* w2, void* preact, void* h, int64_t M,
+                                               int64_t H, int64_t Dout, int dtype, int layout, void* stream) {
+  if (M > 0 && !h) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  return op_grad_preact(grad_y, w2, preact, h, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
 }
 
 int swiglu_b200_forward_logic(const void* preact, void* h, int64_t M, int64_t H, int dtype, int layout,
@@ -1015,7 +1031,7 @@ int swiglu_b200_mlp_backward(const void* x, const void* w1, const void* w2, void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // dW2 reads preact, so it runs before grad_preact overwrites it.
   if (int rc = op_dw2(grad_y, preact, dw2, M, H, Dout, dtype, layout, st)) return rc;
-  if (int rc = op_grad_preact(grad_y, w2, preact, M, H, Dout, dtype, layout, st)) return rc;
+  if (int rc = op_grad_preact(grad_y, w2, preact, nullptr, M, H, Dout, dtype, layout, st)) return rc;
   if (M == 0) {
     const size_t es = dtype == SWIGLU_F32 ? 4 : 2;
     cudaError_t e = cudaMemsetAsync(dw1, 0, (size_t)(2 * H * D) * es, st);

@@ -27,6 +27,9 @@
 //   kEpiDswiglu  backward grad_h GEMM: D = grad_h; reads preact, writes
 //                grad_left / grad_gate over it in place
 //                (swiglu_recompute.py:33-49, fused_forward_packed.py:222-259)
+//                and, if out1 is set, h = left * silu(gate) of the preact it
+//                read into out1 [M, H] (swiglu_recompute.py:71), the operand
+//                of a plain dW2 GEMM
 // The dW2 GEMM with the h prologue is a separate kernel (tc_dw2.cuh).
 #pragma once
 
@@ -341,6 +344,8 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
     // their latency hides behind the TMEM load and the SiLU math.
     const int j0 = pn * BN;
     __nv_bfloat16* pre_row = reinterpret_cast<__nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+    __nv_bfloat16* h_row =
+        p.out1 ? reinterpret_cast<__nv_bfloat16*>(p.out1) + static_cast<long long>(row) * p.ld1 : nullptr;
     uint4 lu[2][4], gu[2][4];
     auto load_chunk = [&](int c, int buf) {
       const int j = j0 + c * 32;
@@ -366,17 +371,20 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
       if (row_ok) {
         const int lc = left_col(j, p.H, p.layout);
         const int gc = gate_col(j, p.H, p.layout);
-        float gl[32], gg[32];
+        // Each group of 8 columns is stored as soon as it is formed (16-byte
+        // stores of grad_left, grad_gate and h), masking columns >= N.
 #pragma unroll
         for (int v8 = 0; v8 < 4; ++v8) {
           const uint32_t lw[4] = {lu[buf][v8].x, lu[buf][v8].y, lu[buf][v8].z, lu[buf][v8].w};
           const uint32_t gw[4] = {gu[buf][v8].x, gu[buf][v8].y, gu[buf][v8].z, gu[buf][v8].w};
+          uint32_t glw[4], ggw[4], hw[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 l2 = unpack_bf16x2(lw[e]);
             const float2 g2 = unpack_bf16x2(gw[e]);
             const float ls[2] = {l2.x, l2.y};
             const float gs[2] = {g2.x, g2.y};
+            float glv[2], ggv[2], hv[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int i = 8 * v8 + 2 * e + u;
@@ -385,13 +393,20 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
               const float sg = sigmoid_fast(gs[u]);
               const float silu = gs[u] * sg;
               const float dsilu = sg + silu * (1.0f - sg);
-              gl[i] = dh * silu;
-              gg[i] = dh * ls[u] * dsilu;
+              glv[u] = dh * silu;
+              ggv[u] = dh * ls[u] * dsilu;
+              hv[u] = ls[u] * silu;  // the dW2 prologue's h, bit for bit
             }
+            glw[e] = pack_bf16x2(glv[0], glv[1]);
+            ggw[e] = pack_bf16x2(ggv[0], ggv[1]);
+            hw[e] = pack_bf16x2(hv[0], hv[1]);
+          }
+          if (j + 8 * v8 + 8 <= p.N) {
+            *reinterpret_cast<uint4*>(pre_row + lc + 8 * v8) = make_uint4(glw[0], glw[1], glw[2], glw[3]);
+            *reinterpret_cast<uint4*>(pre_row + gc + 8 * v8) = make_uint4(ggw[0], ggw[1], ggw[2], ggw[3]);
+            if (h_row) *reinterpret_cast<uint4*>(h_row + j + 8 * v8) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
           }
         }
-        store_row32<false>(pre_row, lc, lc + (p.N - j), gl);
-        store_row32<false>(pre_row, gc, gc + (p.N - j), gg);
       }
     }
   }

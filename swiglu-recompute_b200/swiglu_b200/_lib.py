@@ -41,6 +41,7 @@ _SIGNATURES = {
     "swiglu_b200_matmul_reduce_rows_noalloc": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p],
     "swiglu_b200_bwd_dw2": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
     "swiglu_b200_bwd_grad_preact_inplace": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_bwd_grad_preact_inplace_emit_h": [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
     "swiglu_b200_forward_logic": [_p, _p, _i64, _i64, _i, _i, _p],
     "swiglu_b200_backward_logic": [_p, _p, _p, _i64, _i64, _i, _i, _p],
     "swiglu_b200_pack_weight_chunked": [_p, _p, _i64, _i64, _i64, _i, _i, _p],

@@ -156,16 +156,23 @@ def bwd_dw2(grad_y: torch.Tensor, preact: torch.Tensor, *, layout: int,
 
 
 def bwd_grad_preact_inplace(grad_y: torch.Tensor, w2: torch.Tensor, preact: torch.Tensor, *,
-                            layout: int) -> torch.Tensor:
-    """preact <- grad_preact, from grad_h = grad_y . W2 formed tile by tile (never stored)."""
-    dev = _check_cuda(grad_y, w2, preact)
-    dt = _same_dtype(grad_y, w2, preact)
+                            layout: int, h_out: torch.Tensor | None = None) -> torch.Tensor:
+    """preact <- grad_preact, from grad_h = grad_y . W2 formed tile by tile (never stored).
+    With `h_out` ([M, H]) the same epilogue also writes h = swiglu(preact) of
+    the values it replaces."""
+    dev = _check_cuda(grad_y, w2, preact, h_out)
+    dt = _same_dtype(grad_y, w2, preact, h_out)
     M, Dout = grad_y.shape
     Dout2, H = w2.shape
     assert Dout == Dout2 and preact.shape == (M, 2 * H)
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_bwd_grad_preact_inplace", _p(grad_y), _p(w2), _p(preact), M, H, Dout,
-                  dtype_code(dt), layout, _stream(dev))
+        if h_out is None:
+            _lib.call("swiglu_b200_bwd_grad_preact_inplace", _p(grad_y), _p(w2), _p(preact), M, H, Dout,
+                      dtype_code(dt), layout, _stream(dev))
+        else:
+            assert h_out.shape == (M, H)
+            _lib.call("swiglu_b200_bwd_grad_preact_inplace_emit_h", _p(grad_y), _p(w2), _p(preact),
+                      _p(h_out), M, H, Dout, dtype_code(dt), layout, _stream(dev))
     return preact
 
 

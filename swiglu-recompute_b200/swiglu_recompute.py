@@ -10,10 +10,11 @@ What runs underneath is libswiglu_b200.so (hand-written sm_100a kernels):
   forward   one tcgen05 GEMM whose epilogue writes preact and h
             (h from the bf16-rounded preact, as swiglu_recompute.py:64 does),
             then y = h @ W2.t() on tcgen05; h is a transient buffer.
-  backward  dW2 = grad_y.t() @ h with h recomputed in the GEMM operand prologue;
-            grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
-            written over preact in place (no [M, H] temporaries, no cat);
-            dW1 = grad_preact.t() @ x and dx = grad_preact @ W1 on tcgen05.
+  backward  grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
+            written over preact in place (grad_h never stored, no cat); the
+            same epilogue writes the recomputed h to a transient buffer;
+            dW2 = grad_y.t() @ h, dW1 = grad_preact.t() @ x and
+            dx = grad_preact @ W1 on tcgen05.
 fp32 inputs run the same dataflow on fp32 FFMA kernels (correctness mode).
 
 Shapes:  x [M, D]   W1 [2H, D]   W2 [Dout, H]
@@ -62,11 +63,14 @@ def _flatten_rows(x: torch.Tensor) -> torch.Tensor:
 def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     """Shared backward of the three recompute Functions.
 
-    Order matters: dW2 reads preact, the grad_h GEMM then overwrites preact
-    with grad_preact, and dW1 / dx read grad_preact. preact is internal to the
-    Function (never a graph output), so consuming it is safe; its version
-    counter is bumped so that a second backward through the same graph raises
-    instead of reading grad_preact as preact.
+    The grad_h GEMM overwrites preact with grad_preact in place and, in the
+    same epilogue, writes the recomputed h (swiglu_recompute.py:71) to a
+    transient [M, H] buffer; dW2 = grad_y^T h is then a plain GEMM and h is
+    freed; dW1 / dx read grad_preact. When only dW2 is needed, the dW2 kernel
+    recomputes h in its operand prologue instead (no [M, H] buffer). preact is
+    internal to the Function (never a graph output), so consuming it is safe;
+    its version counter is bumped so that a second backward through the same
+    graph raises instead of reading grad_preact as preact.
     """
     if getattr(ctx, "_preact_consumed", False):
         raise RuntimeError(
@@ -76,12 +80,19 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     gy = _flatten_rows(grad_y)
     if gy.dtype != preact.dtype:
         gy = gy.to(preact.dtype)
-    grad_w2 = ops.bwd_dw2(gy, preact, layout=layout) if need_w2 else None
-    grad_x = grad_w1 = None
-    if need_x or need_w1:
+    grad_x = grad_w1 = grad_w2 = None
+    if not (need_x or need_w1):
+        if need_w2:
+            grad_w2 = ops.bwd_dw2(gy, preact, layout=layout)
+    else:
         ctx._preact_consumed = True
-        gp = ops.bwd_grad_preact_inplace(gy, w2, preact, layout=layout)
+        h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device,
+                        dtype=preact.dtype) if need_w2 else None
+        gp = ops.bwd_grad_preact_inplace(gy, w2, preact, layout=layout, h_out=h)
         torch.autograd.graph.increment_version(preact)
+        if need_w2:
+            grad_w2 = ops.matmul(gy, h, a_t=True, b_t=False)          # [Dout, H] = grad_y^T h
+            del h
         if need_w1:
             if w_form == W1_ROWS:
                 grad_w1 = ops.matmul(gp, x, a_t=True, b_t=False)      # [2H, D] = gp^T x

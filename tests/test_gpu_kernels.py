@@ -117,6 +117,31 @@ def test_grad_preact_inplace(gemm_path, dtype, layout, M, H, Dout):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("layout", [O.STD, O.PACKED])
+@pytest.mark.parametrize("M,H,Dout", [(256, 256, 128), (200, 384, 136), (700, 512, 200), (1024, 768, 640)])
+def test_grad_preact_inplace_emit_h(gemm_path, dtype, layout, M, H, Dout):
+    """The emit-h form writes the same grad_preact as the plain call, h of the
+    replaced preact within the bound, and dW2 = grad_y^T h from it matches the
+    prologue dW2 kernel and the oracle."""
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    gy = _r(M, Dout, seed=12, dtype=dtype).to(DEV)
+    w2 = _r(Dout, H, seed=13, scale=Dout ** -0.5, dtype=dtype).to(DEV)
+    preact = _r(M, 2 * H, seed=14, dtype=dtype)
+    bf = dtype == torch.bfloat16
+    ref_h = O.forward_logic(preact.float(), layout, bf)
+    dw2_prologue = ops.bwd_dw2(gy, preact.to(DEV), layout=lay)
+    plain = ops.bwd_grad_preact_inplace(gy, w2, preact.to(DEV), layout=lay)
+    h = torch.empty((M, H), dtype=dtype, device=DEV)
+    gp = ops.bwd_grad_preact_inplace(gy, w2, preact.to(DEV), layout=lay, h_out=h)
+    assert torch.equal(gp, plain)
+    assert O.rel_max(h.cpu(), ref_h) <= _tol(dtype)
+    dw2 = ops.matmul(gy, h, a_t=True, b_t=False)
+    ref_dw2 = gy.cpu().float().t() @ ref_h
+    assert O.rel_max(dw2.cpu(), ref_dw2) <= _tol(dtype)
+    assert O.rel_max(dw2.cpu(), dw2_prologue.cpu().float()) <= _tol(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("layout", [O.STD, O.PACKED])
 def test_pointwise_kernels(dtype, layout):
     lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
     M, H = 300, 512

@@ -31,7 +31,9 @@ class OracleCompute:
         return gy.t() @ O.forward_logic(preact)
 
     @staticmethod
-    def grad_preact_inplace(gy, w2_local, preact):
+    def grad_preact_inplace(gy, w2_local, preact, h_out=None):
+        if h_out is not None:
+            h_out.copy_(O.forward_logic(preact))
         preact.copy_(O.backward_logic(preact, gy @ w2_local))
         return preact
 
