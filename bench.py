@@ -81,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.index)],
+                 "-lms", "25", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -99,24 +99,29 @@ class ClockSampler:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        """Median SM clock, power and the throttle reasons seen over the samples
+        taken under load (power draw >= 60 % of the highest sample; the sampler
+        also runs a little before and after the timed region)."""
+        rows, mx = [], None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in getattr(self, "lines", []):
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
+                sm, pw = float(parts[1]), float(parts[3])
                 mx = float(parts[2])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+            rows.append((sm, pw, {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        top = max(r[1] for r in rows)
+        loaded = [r for r in rows if r[1] >= 0.6 * top]
+        reasons = set().union(*(r[2] for r in loaded))
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": mx,
+                "power_w": round(statistics.median(r[1] for r in loaded), 1), "reasons": sorted(reasons),
+                "samples": len(rows), "loaded_samples": len(loaded)}
 
 
 # ------------------------------------------------------------- CPU arm
@@ -408,6 +413,22 @@ def run_ours_single(args):
     fl = flops_fwd_bwd(M, D, H, Dout)
     value = fl / (ms * 1e-3) / 1e12
 
+    # The same step with dW2 in the "prologue" mode (h recomputed inside the
+    # dW2 kernel, no [M, H] buffer in backward), timed the same way.
+    ops.set_dw2_mode("prologue")
+    try:
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms_prologue = e0.elapsed_time(e1) / args.steps
+    finally:
+        ops.set_dw2_mode("emit_h")
+
     # End to end through the public API with host buffers: every step copies
     # its x and grad_y in from pinned host memory and its grad_x out, on a copy
     # stream that runs one step ahead (inputs of step i+1 and the output of
@@ -440,6 +461,10 @@ def run_ours_single(args):
                      "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": profile_traffic(dom),
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})"},
         "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
+        "variants": {"dw2_prologue": {"ms_per_step": round(ms_prologue, 4),
+                                      "value": round(fl / (ms_prologue * 1e-3) / 1e12, 2),
+                                      "note": "dW2 with h recomputed in its operand prologue, "
+                                              "no [M, H] buffer in backward"}},
         "clocks": clk.summary(),
     }
     if not args.no_stack:
@@ -447,6 +472,13 @@ def run_ours_single(args):
         line["stacked"] = {"n_blocks": 8, "peak_mib": round(peak, 1), "ms_per_step": round(sms, 3),
                            "reference_recompute_peak_mib": REFERENCE_STACK_PEAK_MIB[8],
                            "method": "max_memory_allocated - base over fwd+grad, min of 3 (as the reference)"}
+        ops.set_dw2_mode("prologue")
+        try:
+            peak_pro, ms_pro = stacked_depth(8, dev)
+        finally:
+            ops.set_dw2_mode("emit_h")
+        line["variants"]["dw2_prologue"]["stacked"] = {"n_blocks": 8, "peak_mib": round(peak_pro, 1),
+                                                       "ms_per_step": round(ms_pro, 3)}
         peak_fc, ms_fc = stacked_depth(8, dev, module="SwiGLUMLPFullCheckpoint")
         line["stacked_full_checkpoint"] = {"n_blocks": 8, "peak_mib": round(peak_fc, 1),
                                            "ms_per_step": round(ms_fc, 3)}

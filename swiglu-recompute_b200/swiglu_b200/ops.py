@@ -52,6 +52,29 @@ def _stream(dev: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(s)
 
 
+# How the backward forms dW2 (read by the recompute Functions and the
+# tensor-parallel block):
+#   "emit_h"    the grad_h GEMM's epilogue also writes h of the preact it
+#               replaces to a transient [M, H] buffer; dW2 = grad_y^T h is a
+#               plain GEMM (fastest; one [M, H] buffer lives from the grad_h
+#               GEMM to the dW2 GEMM);
+#   "prologue"  dW2 recomputes h inside its operand prologue before grad_h
+#               overwrites preact (no [M, H] buffer at all).
+DW2_MODES = ("emit_h", "prologue")
+_dw2_mode = "emit_h"
+
+
+def set_dw2_mode(mode: str) -> None:
+    global _dw2_mode
+    if mode not in DW2_MODES:
+        raise ValueError(f"dW2 mode must be one of {DW2_MODES}, got {mode!r}")
+    _dw2_mode = mode
+
+
+def dw2_mode() -> str:
+    return _dw2_mode
+
+
 def set_stream_k(enabled: bool) -> None:
     """Enables (default) or disables the stream-K tail of the 2-SM GEMMs for
     later calls. Disabling unregisters every workspace this module registered;

@@ -193,13 +193,18 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         x, w1_local, w2_local, preact = ctx.saved_tensors
         compute = ctx.compute
         gy = all_gather_rows(grad_y_local.to(x.dtype), ctx.group)
-        # grad_preact in place of preact; the same epilogue writes the
-        # recomputed h, and dW2 = grad_y^T h is a plain GEMM.
-        h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device, dtype=preact.dtype)
-        gp = compute.grad_preact_inplace(gy, w2_local, preact, h_out=h)
+        # grad_preact in place of preact; dW2 as in the single-GPU backward
+        # (ops.dw2_mode): from the h the same epilogue writes, or with h
+        # recomputed in the dW2 kernel's prologue before preact is replaced.
+        if ops.dw2_mode() == "emit_h":
+            h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device, dtype=preact.dtype)
+            gp = compute.grad_preact_inplace(gy, w2_local, preact, h_out=h)
+            dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
+            del h
+        else:
+            dw2 = compute.dw2(gy, preact)
+            gp = compute.grad_preact_inplace(gy, w2_local, preact)
         torch.autograd.graph.increment_version(preact)
-        dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
-        del h
         dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
         if ctx.fused_rs is not None and ctx.fused_rs.wants(gp.shape[1]):
             dx_local = ctx.fused_rs.matmul("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)

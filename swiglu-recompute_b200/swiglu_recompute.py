@@ -12,9 +12,10 @@ What runs underneath is libswiglu_b200.so (hand-written sm_100a kernels):
             then y = h @ W2.t() on tcgen05; h is a transient buffer.
   backward  grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
             written over preact in place (grad_h never stored, no cat); the
-            same epilogue writes the recomputed h to a transient buffer;
-            dW2 = grad_y.t() @ h, dW1 = grad_preact.t() @ x and
-            dx = grad_preact @ W1 on tcgen05.
+            same epilogue writes the recomputed h to a transient buffer and
+            dW2 = grad_y.t() @ h (or, in the "prologue" dW2 mode, dW2
+            recomputes h inside its operand prologue, no [M, H] buffer);
+            dW1 = grad_preact.t() @ x and dx = grad_preact @ W1 on tcgen05.
 fp32 inputs run the same dataflow on fp32 FFMA kernels (correctness mode).
 
 Shapes:  x [M, D]   W1 [2H, D]   W2 [Dout, H]
@@ -63,14 +64,16 @@ def _flatten_rows(x: torch.Tensor) -> torch.Tensor:
 def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     """Shared backward of the three recompute Functions.
 
-    The grad_h GEMM overwrites preact with grad_preact in place and, in the
-    same epilogue, writes the recomputed h (swiglu_recompute.py:71) to a
-    transient [M, H] buffer; dW2 = grad_y^T h is then a plain GEMM and h is
-    freed; dW1 / dx read grad_preact. When only dW2 is needed, the dW2 kernel
-    recomputes h in its operand prologue instead (no [M, H] buffer). preact is
-    internal to the Function (never a graph output), so consuming it is safe;
-    its version counter is bumped so that a second backward through the same
-    graph raises instead of reading grad_preact as preact.
+    The grad_h GEMM overwrites preact with grad_preact in place; dW1 / dx
+    read grad_preact. dW2 is formed by `ops.dw2_mode()`: "emit_h" (default)
+    has the same grad_h epilogue write the recomputed h (swiglu_recompute.py:71)
+    to a transient [M, H] buffer, and dW2 = grad_y^T h is a plain GEMM;
+    "prologue" runs the dW2 kernel that recomputes h in its operand prologue
+    first, while preact is intact (no [M, H] buffer). When only dW2 is needed
+    the prologue kernel always runs. preact is internal to the Function (never
+    a graph output), so consuming it is safe; its version counter is bumped so
+    that a second backward through the same graph raises instead of reading
+    grad_preact as preact.
     """
     if getattr(ctx, "_preact_consumed", False):
         raise RuntimeError(
@@ -81,16 +84,16 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     if gy.dtype != preact.dtype:
         gy = gy.to(preact.dtype)
     grad_x = grad_w1 = grad_w2 = None
-    if not (need_x or need_w1):
-        if need_w2:
-            grad_w2 = ops.bwd_dw2(gy, preact, layout=layout)
-    else:
+    emit_h = need_w2 and (need_x or need_w1) and ops.dw2_mode() == "emit_h"
+    if need_w2 and not emit_h:
+        grad_w2 = ops.bwd_dw2(gy, preact, layout=layout)
+    if need_x or need_w1:
         ctx._preact_consumed = True
         h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device,
-                        dtype=preact.dtype) if need_w2 else None
+                        dtype=preact.dtype) if emit_h else None
         gp = ops.bwd_grad_preact_inplace(gy, w2, preact, layout=layout, h_out=h)
         torch.autograd.graph.increment_version(preact)
-        if need_w2:
+        if emit_h:
             grad_w2 = ops.matmul(gy, h, a_t=True, b_t=False)          # [Dout, H] = grad_y^T h
             del h
         if need_w1:

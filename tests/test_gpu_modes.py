@@ -5,10 +5,15 @@
 - SwiGLUFullCheckpointFunction saves only x and recomputes preact in backward;
   its outputs and gradients must equal SwiGLUMemoryOptimizedFunction's bit for
   bit, it must not save an [M, 2H] tensor, and its peak memory is lower.
+- The two dW2 modes of the backward ("emit_h": h written by the grad_h
+  epilogue, dW2 a plain GEMM; "prologue": h recomputed in the dW2 kernel's
+  operand prologue) give bit-identical y, dx and dW1 and dW2 within the bf16
+  bound of each other and of the oracle, for every module.
 """
 import pytest
 import torch
 
+from swiglu_b200 import ops
 import fused_forward as FF
 import fused_forward_packed as FP
 import swiglu_recompute as SR
@@ -90,3 +95,26 @@ def test_full_checkpoint_stack_uses_less_memory():
         del model
         torch.cuda.empty_cache()
     assert peaks["SwiGLUMLPFullCheckpoint"] < peaks["SwiGLUMLPCustom"], peaks
+
+
+@pytest.mark.parametrize("M,D,H,Dout", [(512, 384, 640, 256), (1024, 512, 768, 384)])
+def test_dw2_modes_agree(M, D, H, Dout):
+    x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=33, dtype=torch.bfloat16)
+    ref = O.mlp_forward_backward(x.float(), w1.float(), w2.float(), gy.float(), bf16=True)
+    for m in _mods(D, H, Dout, w1, w2):
+        res = {}
+        for mode in ops.DW2_MODES:
+            ops.set_dw2_mode(mode)
+            try:
+                xd = x.cuda().requires_grad_(True)
+                y = m(xd)
+                res[mode] = [y.detach()] + list(torch.autograd.grad(y, [xd] + list(m.parameters()), gy.cuda()))
+            finally:
+                ops.set_dw2_mode("emit_h")
+        a, b = res["emit_h"], res["prologue"]
+        name = type(m).__name__
+        for i in range(3):                        # y, dx, grad of the first-layer weight
+            assert torch.equal(a[i], b[i]), (name, i)
+        assert O.rel_max(a[3].cpu(), b[3].cpu().float()) <= 8e-3, name
+        assert O.rel_max(a[3].cpu(), ref["dw2"]) <= 8e-3, name
+        assert O.rel_max(b[3].cpu(), ref["dw2"]) <= 8e-3, name

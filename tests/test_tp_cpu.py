@@ -44,10 +44,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, D, H, Dout, q):
+def _worker(rank, world, port, M, D, H, Dout, q, dw2_mode="emit_h"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from swiglu_b200 import ops
+        ops.set_dw2_mode(dw2_mode)
         torch.set_num_threads(1)
         x, w1, w2, gy = O.make_inputs(M, D, H, Dout, seed=3)
         ms = M // world
@@ -62,12 +64,14 @@ def _worker(rank, world, port, M, D, H, Dout, q):
 
 
 @pytest.mark.parametrize("world", [2])
-def test_tp_matches_single_rank_oracle(world):
+@pytest.mark.parametrize("dw2_mode", ["emit_h", "prologue"])
+def test_tp_matches_single_rank_oracle(world, dw2_mode):
     M, D, H, Dout = 64, 48, 128, 40
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, H, Dout, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, H, Dout, q, dw2_mode))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
