@@ -523,7 +523,8 @@ def main():
         print(json.dumps(line), flush=True)
         return
     from swiglu_b200 import tp
-    line = tp.bench_tp(args, CFG, flops_fwd_bwd, METRIC, ClockSampler, load_peaks, cpu_reference_sample)
+    line = tp.bench_tp(args, CFG, flops_fwd_bwd, METRIC, ClockSampler, load_peaks, cpu_reference_sample,
+                       e2e_pipelined)
     if line is not None:
         print(json.dumps(line), flush=True)
 

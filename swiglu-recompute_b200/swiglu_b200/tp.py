@@ -75,6 +75,23 @@ def reduce_scatter_rows(t: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class _PendingReduceScatter:
+    """An NCCL reduce-scatter in flight on the collective's own stream; the
+    input stays referenced until `wait` joins the result into the current stream."""
+
+    def __init__(self, t: torch.Tensor, group=None):
+        world = dist.get_world_size(group)
+        assert t.shape[0] % world == 0
+        self.inp = t.contiguous()
+        self.out = torch.empty((t.shape[0] // world, *t.shape[1:]), dtype=t.dtype, device=t.device)
+        self.work = dist.reduce_scatter_tensor(self.out, self.inp, group=group, async_op=True)
+
+    def wait(self) -> torch.Tensor:
+        self.work.wait()
+        self.inp = None
+        return self.out
+
+
 # ------------------------------------------- fused GEMM -> reduce-scatter
 class FusedReduceScatter:
     """Receive buffers in symmetric (peer-mapped) memory for the reduce-scatter
@@ -118,16 +135,23 @@ class FusedReduceScatter:
     # GEMM takes ~2MNK / 1.3 PFLOP/s while (world-1)/world of its 4MN bytes
     # leave at ~0.6 TB/s, i.e. K >= 4333 (world-1) / world. Measured at
     # config 2 (M=11136): world 2 fused 4.60 ms/step vs NCCL 4.96; world 8
-    # (y: K=1792, dx: K=3584) fused 2.18 vs NCCL 2.05.
+    # (y: K=1792, dx: K=3584) fused 2.18 vs NCCL 2.05 (before the backward
+    # deferred dx's reduction behind dW2/dW1; after it 2.03 vs 1.85).
     K_PER_LINK_BYTE = 4333
 
     def wants(self, k):
+        """Whether the scatter GEMM with inner dimension k should carry the
+        reduce-scatter (its math covers its NVLink push). Measured with dx
+        deferred behind dW2/dW1 at world 8 (dx K=3584, below the line):
+        fused 2.03 ms/step vs NCCL 1.85, so the rule holds there too."""
         return k * self.world >= self.K_PER_LINK_BYTE * (self.world - 1)
 
-    def matmul(self, key, a, b, *, a_t, b_t, out_dtype):
-        """Reduce-scattered op(a) . op(b): returns this rank's [M / world, N] rows."""
+    def matmul_start(self, key, a, b, *, a_t, b_t, out_dtype):
+        """Enqueues the scatter GEMM of op(a) . op(b) and its signal; returns a
+        pending handle for `finish`. Work enqueued in between overlaps the
+        other ranks' pushes into this rank's receive buffer."""
         from ._lib import BF16, call
-        from .ops import _p, _stream, dtype_code
+        from .ops import _p, _stream
 
         M = a.shape[1] if a_t else a.shape[0]
         K = a.shape[0] if a_t else a.shape[1]
@@ -137,15 +161,29 @@ class FusedReduceScatter:
         dev = a.device
         recv, _, flags, _, peers, peer_flags = self._slot(key, rows, N, dev)
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
-        out = torch.empty((rows, N), device=dev, dtype=out_dtype)
         st = _stream(dev)
         with torch.cuda.device(dev):
             call("swiglu_b200_matmul_scatter_rows", _p(a), _p(b), M, N, K, int(a_t), int(b_t), BF16,
                  peers, self.world, self.rank, rows, st)
             call("swiglu_b200_tp_signal", peer_flags, self.world, self.rank, self.epoch, st)
-            call("swiglu_b200_tp_reduce_rows", _p(recv), _p(flags), self.world, self.epoch, _p(out), rows, N,
-                 dtype_code(out_dtype), st)
+        return (recv, flags, self.epoch, rows, N, out_dtype, dev)
+
+    def finish(self, pending):
+        """This rank's [M / world, N] rows: the owner's fixed-order sum of the
+        `world` partials, once every rank's signal has arrived."""
+        from ._lib import call
+        from .ops import _p, _stream, dtype_code
+
+        recv, flags, epoch, rows, N, out_dtype, dev = pending
+        out = torch.empty((rows, N), device=dev, dtype=out_dtype)
+        with torch.cuda.device(dev):
+            call("swiglu_b200_tp_reduce_rows", _p(recv), _p(flags), self.world, epoch, _p(out), rows, N,
+                 dtype_code(out_dtype), _stream(dev))
         return out
+
+    def matmul(self, key, a, b, *, a_t, b_t, out_dtype):
+        """Reduce-scattered op(a) . op(b): returns this rank's [M / world, N] rows."""
+        return self.finish(self.matmul_start(key, a, b, a_t=a_t, b_t=b_t, out_dtype=out_dtype))
 
 
 # -------------------------------------------------------- local compute
@@ -196,22 +234,32 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         # grad_preact in place of preact; dW2 as in the single-GPU backward
         # (ops.dw2_mode): from the h the same epilogue writes, or with h
         # recomputed in the dW2 kernel's prologue before preact is replaced.
+        h = None
         if ops.dw2_mode() == "emit_h":
             h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device, dtype=preact.dtype)
             gp = compute.grad_preact_inplace(gy, w2_local, preact, h_out=h)
-            dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
-            del h
         else:
             dw2 = compute.dw2(gy, preact)
             gp = compute.grad_preact_inplace(gy, w2_local, preact)
         torch.autograd.graph.increment_version(preact)
-        dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
-        if ctx.fused_rs is not None and ctx.fused_rs.wants(gp.shape[1]):
-            dx_local = ctx.fused_rs.matmul("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
+        # dx first: its reduce-scatter (the other ranks' pushes and the owner
+        # sum, or NCCL on its own stream) proceeds while dW2 and dW1, which
+        # need no communication, compute.
+        fused = ctx.fused_rs is not None and ctx.fused_rs.wants(gp.shape[1])
+        if fused:
+            pending = ctx.fused_rs.matmul_start("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
         else:
             acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
-            dx_part = compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt)
-            dx_local = reduce_scatter_rows(dx_part, ctx.group).to(x.dtype)
+            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt),
+                                            ctx.group)
+        if h is not None:
+            dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
+            del h
+        dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
+        if fused:
+            dx_local = ctx.fused_rs.finish(pending)
+        else:
+            dx_local = pending.wait().to(x.dtype)
         return dx_local, dw1, dw2, None, None, None, None
 
 
@@ -259,7 +307,7 @@ class SwiGLUMLPTensorParallel(nn.Module):
 
 
 # -------------------------------------------------------------- bench
-def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
+def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e_fn):
     """Strong-scaling TP run of the config-2 block on WORLD_SIZE GPUs (one
     process per GPU). Returns the JSON dict on rank 0, None elsewhere."""
     from oracle.swiglu_oracle import make_inputs
@@ -308,28 +356,11 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         ms = ms.item()
 
-        # End to end with host buffers: this rank's token shard in, its grad_x out.
-        x_h, gy_h = x_l.cpu().pin_memory(), gy_l.cpu().pin_memory()
-        dx_h = torch.empty_like(x_h).pin_memory()
-
-        def e2e_step():
-            xi = x_h.to(dev, non_blocking=True).requires_grad_(True)
-            gyi = gy_h.to(dev, non_blocking=True)
-            y = model(xi)
-            gx = torch.autograd.grad(y, [xi] + params, gyi)[0]
-            dx_h.copy_(gx, non_blocking=True)
-
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2.record(st)
-        for _ in range(args.steps):
-            e2e_step()
-        e3.record(st)
-        torch.cuda.synchronize()
-        e2e_ms = torch.tensor([e2.elapsed_time(e3) / args.steps], device=dev)
+        # End to end with host buffers: this rank's token shard in from pinned
+        # host memory and its grad_x out, on a copy stream one step ahead of
+        # the compute (the single-GPU bench's pipelined loop), max over ranks.
+        e2e_ms, h2d, d2h = e2e_fn(model, params, x_l.cpu(), gy_l.cpu(), dev, args)
+        e2e_ms = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
         e2e_ms = e2e_ms.item()
         status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
@@ -353,8 +384,7 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample):
                        "l2": "working set > L2"},
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": 2 * x_h.numel() * 2 * world,
-                    "d2h_bytes_per_step": dx_h.numel() * 2 * world},
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
             "gpu_launches": 6 * args.steps * world,
             "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
             "device_status": int(status.item()),
