@@ -19,7 +19,7 @@ import functools
 import torch
 import torch.nn as nn
 
-from swiglu_b200 import ops
+from swiglu_b200.library import kernels
 from swiglu_b200.ops import LAYOUT_STD, W1_T
 
 # Reuse this project's own elementwise helpers (fused_forward.py:49 imports them).
@@ -92,8 +92,7 @@ def fused_matmul_swiglu_save_preact(
         f"H={n_half} must be a multiple of {BLOCK_SIZE_N_HALF}"
     )
     # h from the f32 accumulator, as the reference kernel does (fused_forward.py:177).
-    return ops.swiglu_fwd(x, wt, w_form=W1_T, layout=LAYOUT_STD, h_from_rounded=False,
-                          group_size_m=group_size_m)
+    return kernels().swiglu_fwd(x, wt, W1_T, LAYOUT_STD, False, group_size_m)
 
 
 # -----------------------------------------------------------------------------
@@ -108,13 +107,13 @@ class SwiGLUFusedForwardFunction(torch.autograd.Function):
         if not wt.is_contiguous():
             wt = wt.contiguous()
         w2 = w2.contiguous()
+        K = kernels()
         if not any(ctx.needs_input_grad[:3]):                # inference: h only
-            _, h = ops.swiglu_fwd(x, wt, w_form=W1_T, layout=LAYOUT_STD, h_from_rounded=False,
-                                  want_preact=False)
-            return ops.matmul(h, w2, a_t=False, b_t=True)
+            h = K.swiglu_fwd_h(x, wt, W1_T, LAYOUT_STD, False)
+            return K.matmul(h, w2, False, True)
         preact, h = fused_matmul_swiglu_save_preact(x, wt)   # one kernel
         ctx.save_for_backward(x, wt, w2, preact)             # save preact, NOT h
-        y = ops.matmul(h, w2, a_t=False, b_t=True)           # [M, Dout]
+        y = K.matmul(h, w2, False, True)                     # [M, Dout]
         return y
 
     @staticmethod

@@ -24,6 +24,7 @@ import torch
 import torch.nn as nn
 
 from swiglu_b200 import ops
+from swiglu_b200.library import kernels
 from swiglu_b200.ops import LAYOUT_PACKED128, W1_T
 from swiglu_recompute import _recompute_backward
 
@@ -141,8 +142,7 @@ def fused_swiglu_save_preact_packed(x, packed_weight):
     assert k == k2 and n2 % 2 == 0
     n_half = n2 // 2
     assert m % BLOCK_SIZE_M == 0 and n_half % BLOCK_SIZE_N_HALF == 0
-    preact, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
-                               h_from_rounded=False, group_size_m=GROUP_SIZE_M)
+    preact, h = kernels().swiglu_fwd(x, packed_weight, W1_T, LAYOUT_PACKED128, False, GROUP_SIZE_M)
     return h, preact
 
 
@@ -154,9 +154,7 @@ def fused_swiglu_packed_no_save(x, packed_weight):
     m, k = x.shape
     k2, n2 = packed_weight.shape
     assert k == k2 and n2 % 2 == 0 and (n2 // 2) % BLOCK_SIZE_N_HALF == 0
-    _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128, h_from_rounded=False,
-                          want_preact=False, group_size_m=GROUP_SIZE_M)
-    return h
+    return kernels().swiglu_fwd_h(x, packed_weight, W1_T, LAYOUT_PACKED128, False, GROUP_SIZE_M)
 
 
 # -----------------------------------------------------------------------------
@@ -193,13 +191,13 @@ class SwiGLUPackedFusedFunction(torch.autograd.Function):
         if not packed_weight.is_contiguous():
             packed_weight = packed_weight.contiguous()
         w2 = w2.contiguous()
+        K = kernels()
         if not any(ctx.needs_input_grad[:3]):                          # inference: h only
-            _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
-                                  h_from_rounded=False, want_preact=False, group_size_m=GROUP_SIZE_M)
-            return ops.matmul(h, w2, a_t=False, b_t=True)
+            h = K.swiglu_fwd_h(x, packed_weight, W1_T, LAYOUT_PACKED128, False, GROUP_SIZE_M)
+            return K.matmul(h, w2, False, True)
         h, preact = fused_swiglu_save_preact_packed(x, packed_weight)  # one kernel
         ctx.save_for_backward(x, packed_weight, w2, preact)            # save preact, NOT h
-        y = ops.matmul(h, w2, a_t=False, b_t=True)
+        y = K.matmul(h, w2, False, True)
         return y
 
     @staticmethod

@@ -33,7 +33,7 @@ from fused_forward_packed import (  # noqa: F401
     unpack_swiglu_linear_weight,
 )
 from swiglu_b200.ops import LAYOUT_PACKED128, W1_T
-from swiglu_b200 import ops
+from swiglu_b200.library import kernels
 from swiglu_recompute import _recompute_backward
 
 
@@ -47,8 +47,7 @@ def fused_swiglu_save_preact_packed_canon(x, packed_weight):
     assert k == k2 and n2 % 2 == 0
     n_half = n2 // 2
     assert m % BLOCK_SIZE_M == 0 and n_half % BLOCK_SIZE_N_HALF == 0
-    preact, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
-                               h_from_rounded=False, group_size_m=GROUP_SIZE_M)
+    preact, h = kernels().swiglu_fwd(x, packed_weight, W1_T, LAYOUT_PACKED128, False, GROUP_SIZE_M)
     return h, preact
 
 
@@ -60,13 +59,13 @@ class SwiGLUPackedFusedFunctionCanon(torch.autograd.Function):
         if not packed_weight.is_contiguous():
             packed_weight = packed_weight.contiguous()
         w2 = w2.contiguous()
+        K = kernels()
         if not any(ctx.needs_input_grad[:3]):                          # inference: h only
-            _, h = ops.swiglu_fwd(x, packed_weight, w_form=W1_T, layout=LAYOUT_PACKED128,
-                                  h_from_rounded=False, want_preact=False, group_size_m=GROUP_SIZE_M)
-            return ops.matmul(h, w2, a_t=False, b_t=True)
+            h = K.swiglu_fwd_h(x, packed_weight, W1_T, LAYOUT_PACKED128, False, GROUP_SIZE_M)
+            return K.matmul(h, w2, False, True)
         h, preact = fused_swiglu_save_preact_packed_canon(x, packed_weight)
         ctx.save_for_backward(x, packed_weight, w2, preact)
-        return ops.matmul(h, w2, a_t=False, b_t=True)
+        return K.matmul(h, w2, False, True)
 
     @staticmethod
     def backward(ctx, grad_y):

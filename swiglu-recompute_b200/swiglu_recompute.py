@@ -29,6 +29,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from swiglu_b200 import ops
+from swiglu_b200.library import kernels
 from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
 
 
@@ -75,10 +76,12 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     that a second backward through the same graph raises instead of reading
     grad_preact as preact.
     """
-    if getattr(ctx, "_preact_consumed", False):
+    eager = not torch.compiler.is_compiling()
+    if eager and getattr(ctx, "_preact_consumed", False):
         raise RuntimeError(
             "SwiGLU recompute backward was already run for this graph: the saved preact "
             "was consumed in place (retain_graph / double backward is not supported)")
+    K = kernels()
     need_x, need_w1, need_w2 = ctx.needs_input_grad[:3]
     gy = _flatten_rows(grad_y)
     if gy.dtype != preact.dtype:
@@ -86,23 +89,25 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     grad_x = grad_w1 = grad_w2 = None
     emit_h = need_w2 and (need_x or need_w1) and ops.dw2_mode() == "emit_h"
     if need_w2 and not emit_h:
-        grad_w2 = ops.bwd_dw2(gy, preact, layout=layout)
+        grad_w2 = K.bwd_dw2(gy, preact, layout)
     if need_x or need_w1:
-        ctx._preact_consumed = True
         h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device,
                         dtype=preact.dtype) if emit_h else None
-        gp = ops.bwd_grad_preact_inplace(gy, w2, preact, layout=layout, h_out=h)
-        torch.autograd.graph.increment_version(preact)
+        K.bwd_grad_preact_(gy, w2, preact, layout, h)
+        gp = preact                                                   # now holds grad_preact
+        if eager:
+            ctx._preact_consumed = True
+            torch.autograd.graph.increment_version(preact)
         if emit_h:
-            grad_w2 = ops.matmul(gy, h, a_t=True, b_t=False)          # [Dout, H] = grad_y^T h
+            grad_w2 = K.matmul(gy, h, True, False)                    # [Dout, H] = grad_y^T h
             del h
         if need_w1:
             if w_form == W1_ROWS:
-                grad_w1 = ops.matmul(gp, x, a_t=True, b_t=False)      # [2H, D] = gp^T x
+                grad_w1 = K.matmul(gp, x, True, False)                # [2H, D] = gp^T x
             else:
-                grad_w1 = ops.matmul(x, gp, a_t=True, b_t=False)      # [D, 2H] = x^T gp
+                grad_w1 = K.matmul(x, gp, True, False)                # [D, 2H] = x^T gp
         if need_x:
-            grad_x = ops.matmul(gp, w1, a_t=False, b_t=(w_form != W1_ROWS))
+            grad_x = K.matmul(gp, w1, False, w_form != W1_ROWS)
     return grad_x, grad_w1, grad_w2
 
 
@@ -116,11 +121,14 @@ class SwiGLUMemoryOptimizedFunction(torch.autograd.Function):
         x2 = _flatten_rows(x)
         W1c, W2c = W1.contiguous(), W2.contiguous()
         training = any(ctx.needs_input_grad[:3])
+        K = kernels()
         # preact [M, 2H] and the transient h [M, H] from one tcgen05 launch;
         # with no gradient needed, the no-save forward writes h only.
-        preact, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
-                                   want_preact=training)
-        y = ops.matmul(h, W2c, a_t=False, b_t=True)            # [M, Dout] = h W2^T
+        if training:
+            preact, h = K.swiglu_fwd(x2, W1c, W1_ROWS, LAYOUT_STD, True)
+        else:
+            h = K.swiglu_fwd_h(x2, W1c, W1_ROWS, LAYOUT_STD, True)
+        y = K.matmul(h, W2c, False, True)                      # [M, Dout] = h W2^T
         del h                                                 # h is NOT retained
         if training:
             ctx.save_for_backward(x2, W1c, W2c, preact)
@@ -154,9 +162,9 @@ class SwiGLUFullCheckpointFunction(torch.autograd.Function):
         lead = x.shape[:-1]
         x2 = _flatten_rows(x)
         W1c, W2c = W1.contiguous(), W2.contiguous()
-        _, h = ops.swiglu_fwd(x2, W1c, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
-                              want_preact=False)
-        y = ops.matmul(h, W2c, a_t=False, b_t=True)
+        K = kernels()
+        h = K.swiglu_fwd_h(x2, W1c, W1_ROWS, LAYOUT_STD, True)
+        y = K.matmul(h, W2c, False, True)
         del h
         if any(ctx.needs_input_grad[:3]):
             ctx.save_for_backward(x2, W1c, W2c)
@@ -166,8 +174,7 @@ class SwiGLUFullCheckpointFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_y):
         x, W1, W2 = ctx.saved_tensors
-        preact, _ = ops.swiglu_fwd(x, W1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
-                                   want_h=False)
+        preact = kernels().swiglu_fwd_preact(x, W1, W1_ROWS, LAYOUT_STD)
         gx, gw1, gw2 = _recompute_backward(ctx, grad_y, x, W1, W2, preact, w_form=W1_ROWS, layout=LAYOUT_STD)
         if gx is not None:
             gx = gx.reshape(ctx.x_shape)
