@@ -260,6 +260,78 @@ def run_kernel_only(args):
 
 
 REFERENCE_STACK_PEAK_MIB = {1: 2275, 2: 2961, 4: 4334, 8: 7078, 16: 12567}   # results_b200.md:38-42
+REFERENCE_STACK_MS = {1: 8.0, 2: 16.3, 4: 32.9, 8: 55.7, 16: 104.7}             # results_b200.md:38-42
+
+
+def _event_ms(fn, reps=10, warm=3):
+    """Minimum CUDA-event time of one call of `fn` over `reps` calls (each
+    call's operands are larger than the 126 MB L2, so no flush is needed)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best
+
+
+def run_fwd_sweep(args):
+    """Forward-only W1 projection + SwiGLU, BASELINE config 3 (packed weight,
+    D=4096 H=14336, M in {1024, 4096, 16384, 65536}) and the config-2 shape:
+    this library's fused kernel saving preact and h, its no-save form (h only),
+    cuBLAS GEMM + compiled SwiGLU, cuBLAS GEMM alone (the comparison of
+    results_fused_forward.md:75-80). One JSON line per shape; FLOPs 4*M*D*H."""
+    import torch.nn.functional as F
+    from oracle.swiglu_oracle import make_inputs
+    from swiglu_b200 import ops
+    from swiglu_b200.ops import LAYOUT_PACKED128, W1_T
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    for M, D, H in [(1024, 4096, 14336), (4096, 4096, 14336), (16384, 4096, 14336), (65536, 4096, 14336),
+                    (11136, 3584, 14336)]:
+        x, w1, _, _ = make_inputs(M, D, H, 8, seed=0, dtype=torch.bfloat16)
+        x, w1 = x.to(dev), w1.to(dev)
+        wt = w1.t().contiguous()                                     # [D, 2H] standard
+        wp = ops.pack_chunked(wt, 128, unpack=False)                 # [D, 2H] packed
+        act = torch.compile(lambda p, n=H: F.silu(p[:, n:]) * p[:, :n])
+        fns = {
+            "fused_save_packed": lambda: ops.swiglu_fwd(x, wp, w_form=W1_T, layout=LAYOUT_PACKED128,
+                                                        h_from_rounded=False),
+            "fused_nosave_packed": lambda: ops.swiglu_fwd(x, wp, w_form=W1_T, layout=LAYOUT_PACKED128,
+                                                          h_from_rounded=False, want_preact=False),
+            "cublas_gemm_plus_compiled_act": lambda: act(x @ wt),
+            "cublas_gemm": lambda: x @ wt,
+        }
+        ms = {k: _event_ms(f) for k, f in fns.items()}
+        fl = 4.0 * M * D * H
+        print(json.dumps({"sweep": "fwd", "M": M, "D": D, "H": H, "ms": {k: round(v, 4) for k, v in ms.items()},
+                          "tflops": {k: round(fl / (v * 1e-3) / 1e12, 1) for k, v in ms.items()}}), flush=True)
+        del x, w1, wt, wp
+        torch.cuda.empty_cache()
+    from swiglu_b200.ops import device_status
+    assert device_status(0) == 0
+
+
+def run_stack_sweep(args):
+    """Stacked depth: N in {1, 2, 4, 8, 16} config-2 blocks,
+    peak memory and ms per fwd+bwd as the reference measures them, for the
+    recompute module and the full-checkpoint module. One JSON line per N."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    for n in (1, 2, 4, 8, 16):
+        peak, ms = stacked_depth(n, dev)
+        peak_fc, ms_fc = stacked_depth(n, dev, module="SwiGLUMLPFullCheckpoint")
+        print(json.dumps({"sweep": "stack", "n_blocks": n,
+                          "recompute": {"peak_mib": round(peak, 1), "ms_per_step": round(ms, 3)},
+                          "full_checkpoint": {"peak_mib": round(peak_fc, 1), "ms_per_step": round(ms_fc, 3)},
+                          "reference_recompute": {"peak_mib": REFERENCE_STACK_PEAK_MIB[n],
+                                                  "ms_per_step": REFERENCE_STACK_MS[n]}}), flush=True)
 
 
 def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom"):
@@ -501,6 +573,10 @@ def main():
     ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "dw2gemm", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--fwd-sweep", action="store_true",
+                    help="forward-only W1 projection + SwiGLU vs cuBLAS, config 3 M sweep (not the bench line)")
+    ap.add_argument("--stack-sweep", action="store_true",
+                    help="stacked-depth memory and time at N = 1..16 blocks, config 4 (not the bench line)")
     ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2], default=0,
                     help="tcgen05 kernel family: 0 by size, 1 single-SM, 2 CTA pair")
     args = ap.parse_args()
@@ -514,6 +590,12 @@ def main():
         _lib.set_gemm_path(args.gemm_path)
     if args.kernel:
         run_kernel_only(args)
+        return
+    if args.fwd_sweep:
+        run_fwd_sweep(args)
+        return
+    if args.stack_sweep:
+        run_stack_sweep(args)
         return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
