@@ -166,7 +166,7 @@ def run_reference_arm(args, rank, world):
 
 # ------------------------------------------------------------- GPU arm
 def _inputs(dev, dtype=torch.bfloat16):
-    from oracle.swiglu_oracle import make_inputs
+    from swiglu_b200.synthetic import make_inputs
     x, w1, w2, gy = make_inputs(CFG["M"], CFG["D"], CFG["H"], CFG["Dout"], seed=0, dtype=dtype)
     return x, w1, w2, gy
 
@@ -287,7 +287,7 @@ def run_fwd_sweep(args):
     cuBLAS GEMM + compiled SwiGLU, cuBLAS GEMM alone (the comparison of
     results_fused_forward.md:75-80). One JSON line per shape; FLOPs 4*M*D*H."""
     import torch.nn.functional as F
-    from oracle.swiglu_oracle import make_inputs
+    from swiglu_b200.synthetic import make_inputs
     from swiglu_b200 import ops
     from swiglu_b200.ops import LAYOUT_PACKED128, W1_T
 
@@ -321,28 +321,36 @@ def run_fwd_sweep(args):
 def run_stack_sweep(args):
     """Stacked depth: N in {1, 2, 4, 8, 16} config-2 blocks,
     peak memory and ms per fwd+bwd as the reference measures them, for the
-    recompute module and the full-checkpoint module. One JSON line per N."""
+    recompute module, the full-checkpoint module and, on the same GPU, the
+    torch.compile'd standard MLP (cuBLAS GEMMs + Inductor pointwise, the
+    reference's fair baseline). One JSON line per N."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     for n in (1, 2, 4, 8, 16):
         peak, ms = stacked_depth(n, dev)
         peak_fc, ms_fc = stacked_depth(n, dev, module="SwiGLUMLPFullCheckpoint")
+        peak_gt, ms_gt = stacked_depth(n, dev, module="SwiGLUMLPGroundTruth", compile_model=True)
+        torch._dynamo.reset()
         print(json.dumps({"sweep": "stack", "n_blocks": n,
                           "recompute": {"peak_mib": round(peak, 1), "ms_per_step": round(ms, 3)},
                           "full_checkpoint": {"peak_mib": round(peak_fc, 1), "ms_per_step": round(ms_fc, 3)},
+                          "standard_mlp_compiled_same_box": {"peak_mib": round(peak_gt, 1),
+                                                             "ms_per_step": round(ms_gt, 3)},
                           "reference_recompute": {"peak_mib": REFERENCE_STACK_PEAK_MIB[n],
                                                   "ms_per_step": REFERENCE_STACK_MS[n]}}), flush=True)
 
 
-def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom"):
+def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom", compile_model=False):
     """Peak allocated-memory delta (MiB) and ms per fwd+bwd of `n_blocks`
     stacked config-2 blocks, measured as the reference's stacked-depth
     benchmark does (bench_stacked_blocks.py:55-102): two warm-up steps, then
     per rep reset the peak counter, record the base allocation, run forward
     through all blocks plus one autograd.grad, take peak - base; min over reps.
-    Block i's weights are seeded with seed 1 + i."""
+    Block i's weights are seeded with seed 1 + i. `compile_model` wraps the
+    stack in torch.compile (the reference's fair baseline does so for the
+    standard MLP, bench_fair_compile.py:45)."""
     import swiglu_recompute as SR
-    from oracle.swiglu_oracle import make_inputs
+    from swiglu_b200.synthetic import make_inputs
 
     M, D, H = CFG["M"], CFG["D"], CFG["H"]
     blocks = []
@@ -355,6 +363,8 @@ def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom"):
         blocks.append(b)
     model = torch.nn.Sequential(*blocks)
     params = list(model.parameters())
+    if compile_model:
+        model = torch.compile(model)
     x0, _, _, _ = make_inputs(M, D, 1, 1, seed=0, dtype=torch.bfloat16)
     g = torch.Generator().manual_seed(7)
     x0 = x0.to(dev)

@@ -310,7 +310,7 @@ class SwiGLUMLPTensorParallel(nn.Module):
 def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e_fn):
     """Strong-scaling TP run of the config-2 block on WORLD_SIZE GPUs (one
     process per GPU). Returns the JSON dict on rank 0, None elsewhere."""
-    from oracle.swiglu_oracle import make_inputs
+    from swiglu_b200.synthetic import make_inputs
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -3,6 +3,7 @@ rejects bad arguments before touching the device. CPU only (no compute calls).""
 import ctypes
 
 import pytest
+import torch
 
 from swiglu_b200 import _lib
 
@@ -74,3 +75,14 @@ def test_check_raises_with_detail(lib):
     rc = lib.swiglu_b200_bwd_dw2(_p(0), _p(16), _p(16), 8, 8, 8, 1, 0, _p(0))
     with pytest.raises(_lib.SwigluError, match="SWIGLU_ERR_INVALID_ARGUMENT: null pointer"):
         _lib.check(rc)
+
+
+def test_synthetic_inputs_match_the_oracle_draw():
+    """bench.py and the TP bench draw their inputs with swiglu_b200.synthetic,
+    the tests with the oracle's copy: same seed, same bits."""
+    from oracle import swiglu_oracle as O
+    from swiglu_b200.synthetic import make_inputs
+
+    for shape, seed, dtype in [((64, 48, 40, 24), 0, torch.float32), ((33, 16, 8, 8), 7, torch.bfloat16)]:
+        for a, b in zip(make_inputs(*shape, seed=seed, dtype=dtype), O.make_inputs(*shape, seed=seed, dtype=dtype)):
+            assert torch.equal(a, b)
