@@ -263,20 +263,23 @@ REFERENCE_STACK_PEAK_MIB = {1: 2275, 2: 2961, 4: 4334, 8: 7078, 16: 12567}   # r
 REFERENCE_STACK_MS = {1: 8.0, 2: 16.3, 4: 32.9, 8: 55.7, 16: 104.7}             # results_b200.md:38-42
 
 
-def _event_ms(fn, reps=10, warm=3):
-    """Minimum CUDA-event time of one call of `fn` over `reps` calls (each
-    call's operands are larger than the 126 MB L2, so no flush is needed)."""
-    for _ in range(warm):
-        fn()
+def _event_ms_interleaved(fns, reps=12, warm=3):
+    """Minimum CUDA-event time of one call of each of `fns` ({name: fn}); the
+    variants take turns call by call, so each sees the same power and
+    thermal state (each call's operands exceed the 126 MB L2, so no flush)."""
+    for fn in fns.values():
+        for _ in range(warm):
+            fn()
     torch.cuda.synchronize()
-    best = float("inf")
+    best = {k: float("inf") for k in fns}
     for _ in range(reps):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        fn()
-        e1.record()
-        torch.cuda.synchronize()
-        best = min(best, e0.elapsed_time(e1))
+        for k, fn in fns.items():
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            best[k] = min(best[k], e0.elapsed_time(e1))
     return best
 
 
@@ -308,7 +311,7 @@ def run_fwd_sweep(args):
             "cublas_gemm_plus_compiled_act": lambda: act(x @ wt),
             "cublas_gemm": lambda: x @ wt,
         }
-        ms = {k: _event_ms(f) for k, f in fns.items()}
+        ms = _event_ms_interleaved(fns)
         fl = 4.0 * M * D * H
         print(json.dumps({"sweep": "fwd", "M": M, "D": D, "H": H, "ms": {k: round(v, 4) for k, v in ms.items()},
                           "tflops": {k: round(fl / (v * 1e-3) / 1e12, 1) for k, v in ms.items()}}), flush=True)
