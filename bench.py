@@ -590,8 +590,8 @@ def main():
                     help="forward-only W1 projection + SwiGLU vs cuBLAS, config 3 M sweep (not the bench line)")
     ap.add_argument("--stack-sweep", action="store_true",
                     help="stacked-depth memory and time at N = 1..16 blocks, config 4 (not the bench line)")
-    ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2], default=0,
-                    help="tcgen05 kernel family: 0 by size, 1 single-SM, 2 CTA pair")
+    ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2, 3], default=0,
+                    help="tcgen05 kernel family: 0 by size, 1 single-SM, 2 CTA pair 256x256, 3 CTA pair 256x512")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -68,7 +68,9 @@ int swiglu_b200_device_status(uint32_t* bits, int clear);
 
 /* Selects the tcgen05 GEMM kernel family for subsequent calls (process-wide):
  * 0 = by problem size (default), 1 = single-SM kernel (128-row tiles),
- * 2 = 2-SM kernel (cta_group::2, 256-row tiles on a CTA pair).
+ * 2 = 2-SM kernel (cta_group::2, 256 x 256 tiles on a CTA pair),
+ * 3 = 2-SM kernel with 256 x 512 tiles (one accumulator filling TMEM).
+ * The dW2 prologue kernel has no 256 x 512 form (3 selects its 2-SM kernel).
  * Results are identical up to f32 summation order; this exists for testing
  * and tuning. No reference counterpart (the reference's Triton kernels pick
  * their tiling at compile time, fused_forward.py:55-65). */

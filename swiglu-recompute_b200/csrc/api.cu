@@ -161,6 +161,26 @@ int make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, ui
   return SWIGLU_OK;
 }
 
+// Output map of a store GEMM: row-major [M, N] (pitch ld elements) in
+// {32 x 32} boxes, 64-byte swizzle for bf16 rows of 64 bytes, 128-byte for f32.
+int make_store_map(CUtensorMap* m, void* ptr, uint64_t N, uint64_t M, uint64_t ld, bool f32) {
+  EncodeTiledFn fn;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  const uint64_t es = f32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16) return fail(SWIGLU_ERR_MISALIGNED, "C: base address is not 16-byte aligned");
+  if ((ld * es) % 16) return fail(SWIGLU_ERR_MISALIGNED, "C: row pitch is not a multiple of 16 bytes");
+  const cuuint64_t dims[2] = {N, M};
+  const cuuint64_t strides[1] = {ld * es};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
+                  box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SWIGLU_ERR_CUDA, "C: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return SWIGLU_OK;
+}
+
 // Operand maps. K-major operand stored [rows][K]; MN-major stored [K][cols].
 int map_kmajor(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows,
                const char* what) {
@@ -174,7 +194,8 @@ int map_mnmajor(CUtensorMap* m, const void* p, int64_t K, int64_t cols, int64_t 
 constexpr uint32_t kMnLbo = 64 * 64 * 2;  // one {64, 64} bf16 box
 constexpr uint32_t kMnSbo = 8 * 128;      // eight 128-byte swizzle rows
 
-// GEMM kernel choice: 0 = by size, 1 = single-SM kernel, 2 = 2-SM kernel.
+// GEMM kernel choice: 0 = by size, 1 = single-SM kernel, 2 = 2-SM kernel with
+// 256 x 256 tiles, 3 = 2-SM kernel with 256 x 512 tiles.
 std::atomic<int> g_gemm_path{0};
 
 // Per-kernel launch state: dynamic shared memory opt-in done (bit per device)
@@ -396,11 +417,15 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
   int mode = g_gemm_path.load(std::memory_order_relaxed);
   // By size: pairs pay off once there is at least one full wave of them.
   if (mode == 0) mode = tiles2 >= d.sms / 2 ? 2 : 1;
-  if (mode == 2) {
+  if (mode == 2 || mode == 3) {
     // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
     // fused_forward.py:58); a pair tile covers two of them.
     p.tiles_m = (p.M + 255) / 256;
     p.group_m = p.group_m > 1 ? p.group_m / 2 : 1;
+    if (mode == 3) {  // 256 x 512 pair tiles: twice the columns per tile
+      p.tiles_n = (p.tiles_n + 1) / 2;
+      return launch_tc2<Tc2Cfg<A_MN, B_MN, EPI, F32, 2>>(p, d, st);
+    }
     return launch_tc2<Tc2Cfg<A_MN, B_MN, EPI, F32>>(p, d, st);
   }
   p.tiles_m = (p.M + 127) / 128;
@@ -550,12 +575,13 @@ int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64
     if (int rc = map_kmajor(&p.tmB, b, N, K, K, 128, "B")) return rc;
   }
   if (reinterpret_cast<uintptr_t>(c) % 16) return fail(SWIGLU_ERR_MISALIGNED, "C must be 16-byte aligned");
+  const bool f32 = out_dtype == SWIGLU_F32;
+  if (int rc = make_store_map(&p.tmC, c, N, M, N, f32)) return rc;
   p.out0 = c;
   p.ld0 = N;
   p.M = (int)M, p.N = (int)N, p.K = (int)K, p.H = 0, p.layout = 0;
   p.tiles_n = (int)((N + 255) / 256);
   p.group_m = group_m;
-  const bool f32 = out_dtype == SWIGLU_F32;
 #define SWIGLU_MM(AM, BM_, F) run_gemm<AM, BM_, kEpiStore, F>(p, *d, st)
   if (f32) {
     if (a_mn) return b_mn ? SWIGLU_MM(true, true, true) : SWIGLU_MM(true, false, true);
@@ -704,7 +730,7 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   const int pair_tiles = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ) * p.tiles_d;
   int mode = g_gemm_path.load(std::memory_order_relaxed);
   if (mode == 0) mode = pair_tiles >= d->sms / 2 ? 2 : 1;
-  if (mode == 2) {
+  if (mode >= 2) {
     p.tiles_j = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ);
     const char* what = "dW2 (CTA pair)";
     int cap = 0;
@@ -958,7 +984,7 @@ int swiglu_b200_set_stream_workspace(void* workspace, size_t bytes, void* stream
 }
 
 int swiglu_b200_set_gemm_path(int mode) {
-  if (mode < 0 || mode > 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "gemm path must be 0, 1 or 2");
+  if (mode < 0 || mode > 3) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "gemm path must be 0, 1, 2 or 3");
   g_gemm_path.store(mode);
   return SWIGLU_OK;
 }

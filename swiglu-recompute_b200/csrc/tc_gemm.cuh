@@ -55,6 +55,7 @@ __host__ __device__ __forceinline__ int gate_col(int j, int H, int layout) {
 struct TcParams {
   CUtensorMap tmA;  // A operand (box: K-major {64,128} / MN-major {64,64})
   CUtensorMap tmB;  // B operand (box: K-major {64,BN/2} / MN-major {64,64})
+  CUtensorMap tmC;  // output [M, N], {32 x 32} boxes: the TMA-store epilogue (2-SM kernel, kEpiStore)
   void* out0;       // store: D; swiglu: preact; dswiglu: preact (in/out)
   void* out1;       // swiglu: h (may be null)
   long long ld0, ld1;
@@ -252,6 +253,62 @@ __device__ __forceinline__ void store_row32(void* row_ptr, int c0, int ncols, co
 // Epilogue of one output tile for the 32 rows of one warp: row `row` of the
 // output (this thread's TMEM lane) and its TMEM address `t_row` (lane base +
 // accumulator column base). Tile (pm, pn) of BN accumulator columns.
+// Store epilogue through shared memory and TMA (2-SM kernel): each warp
+// turns 32 accumulator columns of its 32 rows into a {32 x 32} box in one of
+// two swizzled shared-memory buffers and one lane issues a TMA store of the
+// box, so the output leaves as whole lines instead of 16 bytes of 32 rows per
+// store instruction. Box rows are 64 bytes (bf16, 64-byte swizzle: 16-byte
+// chunk c of row r at c ^ ((r >> 1) & 3)) or 128 bytes (f32, 128-byte
+// swizzle: chunk c at c ^ (r & 7)); either way a warp's 16-byte writes take
+// the minimum four wavefronts. `stage` is 1024-byte aligned, two boxes.
+template <bool OUT_F32>
+struct StoreStage {
+  static constexpr int kRowBytes = OUT_F32 ? 128 : 64;
+  static constexpr int kBoxBytes = 32 * kRowBytes;
+  static constexpr int kWarpBytes = 2 * ((kBoxBytes + 1023) / 1024) * 1024;
+};
+
+template <int BN, bool OUT_F32>
+__device__ __forceinline__ void epilogue_store_tma(const TcParams& p, int pn, int row0, uint32_t t_row,
+                                                   uint8_t* stage) {
+  using S = StoreStage<OUT_F32>;
+  constexpr int kChunks16 = S::kRowBytes / 16;  // 16-byte chunks per box row
+  const uint32_t lane = threadIdx.x & 31u;
+  const int n0 = pn * BN;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    tmem_ld_wait();
+    uint8_t* buf = stage + (c & 1) * (S::kWarpBytes / 2);
+    // The store issued from this buffer two chunks ago (possibly in the
+    // previous tile) has read it once at most one store is still reading.
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    uint8_t* row_base = buf + lane * S::kRowBytes;
+#pragma unroll
+    for (int k = 0; k < kChunks16; ++k) {
+      uint4 v;
+      if constexpr (OUT_F32) {
+        v = make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+      } else {
+        v = make_uint4(pack_bf16x2(__uint_as_float(r[8 * k]), __uint_as_float(r[8 * k + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * k + 2]), __uint_as_float(r[8 * k + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * k + 4]), __uint_as_float(r[8 * k + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * k + 6]), __uint_as_float(r[8 * k + 7])));
+      }
+      const int kk = OUT_F32 ? (k ^ static_cast<int>(lane & 7u)) : (k ^ static_cast<int>((lane >> 1) & 3u));
+      *reinterpret_cast<uint4*>(row_base + 16 * kk) = v;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&p.tmC, buf, n0 + c * 32, row0);
+      bulk_commit();
+    }
+  }
+}
+
 template <int BN, int EPI, bool OUT_F32>
 __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn, int row, uint32_t t_row,
                                               float* stage = nullptr) {

@@ -1,11 +1,13 @@
 // 2-SM (cta_group::2) variant of the persistent warp-specialized GEMM.
 //
-// A cluster of two CTAs on neighbouring SMs computes one 256 x 256 output
-// tile with M=256 tcgen05.mma instructions issued by rank 0. Each CTA stages
-// only its half of the operands (A rows [128r, 128r+128) and B columns
-// [128r, 128r+128)) and its TMEM receives its 128 rows of D, so per SM the
-// shared-memory footprint per MMA-clock and the L2 operand traffic are half
-// those of the single-SM kernel (tc_gemm.cuh): 6 pipeline stages fit.
+// A cluster of two CTAs on neighbouring SMs computes one 256 x (256·NSUB)
+// output tile with M=256, N=256 tcgen05.mma instructions issued by rank 0
+// (NSUB of them per 16-deep k-step). Each CTA stages only its half of the
+// operands (A rows [128r, 128r+128) and, of each MMA's 256 B columns, the
+// 128 at [128r, 128r+128)) and its TMEM receives its 128 rows of D, so per
+// SM the shared-memory footprint per MMA-clock and the L2 operand traffic are
+// half those of the single-SM kernel (tc_gemm.cuh); with NSUB = 2 a further
+// quarter less (see Tc2Cfg).
 //
 // Protocol (all waits bounded):
 //   both CTAs' producers wait on their own `empty[s]` and TMA-load their halves
@@ -24,25 +26,38 @@
 
 namespace swiglu {
 
-template <bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
+// NSUB = N=256 MMAs per k-step: 1 gives 256 x 256 pair tiles with the
+// accumulator double-buffered in TMEM (the epilogue of one tile overlaps the
+// next tile's main loop); 2 gives 256 x 512 pair tiles whose single
+// accumulator fills the CTA's 512 TMEM columns: per MMA FLOP a CTA then loads
+// 25 % fewer operand bytes from L2 (A is shared by both N halves), and the
+// epilogue runs between main loops while TMA keeps filling the ring.
+template <bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_, int NSUB_ = 1>
 struct Tc2Cfg {
-  static constexpr int BM = 256;   // pair tile rows (128 per CTA)
-  static constexpr int BMH = 128;  // rows per CTA
-  static constexpr int BN = 256;   // tile columns (128 of B per CTA)
+  static constexpr int NSUB = NSUB_;
+  static_assert(NSUB == 1 || NSUB == 2, "one or two N=256 MMAs per k-step");
+  static constexpr int BM = 256;          // pair tile rows (128 per CTA)
+  static constexpr int BMH = 128;         // rows per CTA
+  static constexpr int BN = 256 * NSUB;   // tile columns (BN / 2 of B per CTA)
   static constexpr int BK = 64;
   static constexpr bool A_MN = A_MN_;
   static constexpr bool B_MN = B_MN_;
   static constexpr int EPI = EPI_;
   static constexpr bool OUT_F32 = OUT_F32_;
-  static constexpr int A_BYTES = BMH * BK * 2;      // 16 KB
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB
+  static constexpr int A_BYTES = BMH * BK * 2;         // 16 KB
+  static constexpr int SUB_B_BYTES = 128 * BK * 2;     // 16 KB: this CTA's half of one N=256 MMA's B
+  static constexpr int B_BYTES = NSUB * SUB_B_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = NSUB == 1 ? 6 : 4;
+  static constexpr int ACCS = NSUB == 1 ? 2 : 1;       // accumulator buffers in TMEM
+  static constexpr int TMEM_COLS = 512;
   static constexpr int NUM_THREADS = 192;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
-  static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4 : 0;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + EPI_STAGE_BYTES;
+  static constexpr int EPI_STAGE_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
+  static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4
+                                         : EPI == kEpiStore     ? 4 * StoreStage<OUT_F32>::kWarpBytes
+                                                                : 0;
+  static constexpr int SMEM_BYTES = 1024 + EPI_STAGE_OFFSET + EPI_STAGE_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -104,12 +119,23 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         int pm, pn;
         tile_coords(w.tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
         const int m0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank);
-        int b0;  // first column of this CTA's half of B
-        if constexpr (Cfg::EPI == kEpiSwiglu) {
-          const int j0 = pn * (BN / 2);
-          b0 = leader ? left_col(j0, p.H, p.layout) : gate_col(j0, p.H, p.layout);
-        } else {
-          b0 = pn * BN + (BN / 2) * static_cast<int>(rank);
+        // First B column of this CTA's 128-column half of each N=256 MMA.
+        int b0[Cfg::NSUB];
+#pragma unroll
+        for (int sub = 0; sub < Cfg::NSUB; ++sub) {
+          if constexpr (Cfg::EPI == kEpiSwiglu) {
+            // Accumulator columns [0, BN/2) are left units, [BN/2, BN) gate
+            // units of the tile's BN/2 hidden units j0...
+            const int j0 = pn * (BN / 2);
+            if constexpr (Cfg::NSUB == 1) {  // ...rank 0 holds the left half, rank 1 the gate half
+              b0[sub] = leader ? left_col(j0, p.H, p.layout) : gate_col(j0, p.H, p.layout);
+            } else {  // ...MMA 0 the left units, MMA 1 the gate units, split by rank
+              const int j = j0 + 128 * static_cast<int>(rank);
+              b0[sub] = sub == 0 ? left_col(j, p.H, p.layout) : gate_col(j, p.H, p.layout);
+            }
+          } else {
+            b0[sub] = pn * BN + 256 * sub + 128 * static_cast<int>(rank);
+          }
         }
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, status, kErrTimeoutProducer)) {
@@ -127,11 +153,15 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
           } else {
             tma_load_2d_pair(sa, &p.tmA, bar, k0, m0);
           }
-          if constexpr (Cfg::B_MN) {
-            tma_load_2d_pair(sb, &p.tmB, bar, b0, k0);
-            tma_load_2d_pair(sb + 64 * BK * 2, &p.tmB, bar, b0 + 64, k0);
-          } else {
-            tma_load_2d_pair(sb, &p.tmB, bar, k0, b0);
+#pragma unroll
+          for (int sub = 0; sub < Cfg::NSUB; ++sub) {
+            uint8_t* sbs = sb + sub * Cfg::SUB_B_BYTES;
+            if constexpr (Cfg::B_MN) {
+              tma_load_2d_pair(sbs, &p.tmB, bar, b0[sub], k0);
+              tma_load_2d_pair(sbs + 64 * BK * 2, &p.tmB, bar, b0[sub] + 64, k0);
+            } else {
+              tma_load_2d_pair(sbs, &p.tmB, bar, k0, b0[sub]);
+            }
           }
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
@@ -151,7 +181,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc_f16(256, BN, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
+      constexpr uint32_t idesc = make_idesc_f16(256, 256, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (int u = first_unit; u < num_units && ok; u += unit_step) {
@@ -171,9 +201,13 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
                                              : make_smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sb + k * 2048, p.mn_lbo, p.mn_sbo)
-                                             : make_smem_desc_sw128(sb + k * 32, 16, 1024);
-            umma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
+#pragma unroll
+            for (int sub = 0; sub < Cfg::NSUB; ++sub) {
+              const uint32_t sbs = sb + sub * Cfg::SUB_B_BYTES;
+              const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sbs + k * 2048, p.mn_lbo, p.mn_sbo)
+                                               : make_smem_desc_sw128(sbs + k * 32, 16, 1024);
+              umma_f16_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
+            }
           }
           umma_commit_pair(map_to_rank(&empty[stage], 0));
           umma_commit_pair(map_to_rank(&empty[stage], 1));
@@ -185,7 +219,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         if (!ok) break;
         umma_commit_pair(map_to_rank(&tmem_full[acc], 0));
         umma_commit_pair(map_to_rank(&tmem_full[acc], 1));
-        if (++acc == 2) {
+        if (++acc == Cfg::ACCS) {
           acc = 0;
           acc_phase ^= 1;
         }
@@ -206,10 +240,18 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       const int row_in_tile = Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
       const int row = pm * Cfg::BM + row_in_tile;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16) + acc * BN;
-      float* stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES) +
-                     (warp - 2) * kScatterStageFloats;
+      float* stage = reinterpret_cast<float*>(smem + Cfg::EPI_STAGE_OFFSET) + (warp - 2) * kScatterStageFloats;
+      uint8_t* store_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * StoreStage<Cfg::OUT_F32>::kWarpBytes;
+      const int row0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32);
+      auto finish_tile = [&]() {
+        if constexpr (Cfg::EPI == kEpiStore) {
+          epilogue_store_tma<BN, Cfg::OUT_F32>(p, pn, row0, t_row, store_stage);
+        } else {
+          epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+        }
+      };
       if (w.parts == 1) {
-        epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+        finish_tile();
       } else {
         // Stream-K part: the last of the parts to arrive for this 32-row
         // slab finishes the tile.
@@ -218,15 +260,19 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         const float* fix = p.sk_partials + (static_cast<long long>(i) * w.parts * Cfg::BM + row_in_tile) * BN;
         if (sk_publish_and_fix(t_row, BN, const_cast<float*>(fix) + w.part * part_stride, fix, part_stride, w.parts,
                                p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch))
-          epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+          finish_tile();
       }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[acc], 0));
-      if (++acc == 2) {
+      if (++acc == Cfg::ACCS) {
         acc = 0;
         acc_phase ^= 1;
       }
+    }
+    // The TMA stores read shared memory asynchronously: finish before exit.
+    if constexpr (Cfg::EPI == kEpiStore) {
+      if (lane == 0) bulk_wait_read<0>();
     }
   }
 

@@ -107,7 +107,8 @@ def call(name: str, *args) -> None:
 
 
 def set_gemm_path(mode: int) -> None:
-    """0 = by size, 1 = single-SM tcgen05 kernel, 2 = 2-SM (CTA pair) kernel."""
+    """0 = by size, 1 = single-SM tcgen05 kernel, 2 = 2-SM (CTA pair) kernel with 256 x 256
+    tiles, 3 = 2-SM kernel with 256 x 512 tiles."""
     call("swiglu_b200_set_gemm_path", int(mode))
 
 

@@ -18,7 +18,7 @@ F32_TOL = 1e-5
 DEV = "cuda"
 
 
-@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+@pytest.fixture(params=[1, 2, 3], ids=["1sm", "2sm", "2sm_n512"])
 def gemm_path(request):
     """Run the bf16 GEMMs on the single-SM kernel and on the 2-SM (CTA pair) kernel."""
     _lib.set_gemm_path(request.param)

@@ -26,9 +26,9 @@ DEV = "cuda"
 COUNTER_WORDS = 1024  # the workspace's first 4096 bytes
 
 
-@pytest.fixture
-def pair_path():
-    _lib.set_gemm_path(2)
+@pytest.fixture(params=[2, 3], ids=["n256", "n512"])
+def pair_path(request):
+    _lib.set_gemm_path(request.param)
     yield
     _lib.set_gemm_path(0)
     ops.set_stream_k(True)
@@ -74,8 +74,8 @@ def _check(results, ref):
 
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
-@pytest.mark.parametrize("M,N,K", [(512, 768, 2048),      # 6 tiles, all split 4 ways
-                                   (2560, 2048, 512)])    # 80 tiles: a full round + 6 split 2 ways
+@pytest.mark.parametrize("M,N,K", [(512, 768, 2048),      # 6 (n256) or 4 (n512) tiles, all split 4 ways
+                                   (2560, 4096, 512)])    # 160 / 80 tiles: full rounds + 12 / 6 split 2 ways
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_matmul_stream_k(pair_path, a_t, b_t, M, N, K, out_dtype):
     a = _r(*((K, M) if a_t else (M, K)), seed=1)
