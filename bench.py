@@ -196,9 +196,9 @@ def kernel_breakdown(x, w1, w2, gy, iters):
         dw2 = ops.matmul(gy, h, a_t=True, b_t=False)
         ev[4].record(st)
         del h
-        dw1 = ops.matmul(preact, x, a_t=True, b_t=False)
+        dw1 = ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512)
         ev[5].record(st)
-        dx = ops.matmul(preact, w1, a_t=False, b_t=False)
+        dx = ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512)
         ev[6].record(st)
         del preact, dw2, dw1, dx
         evs.append(ev)
@@ -236,8 +236,8 @@ def run_kernel_only(args):
         "dw2gemm": lambda: ops.matmul(gy, h, a_t=True, b_t=False),
         # in place on a scratch copy so repeated launches see the same input
         "gradh": lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD, h_out=h),
-        "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False),
-        "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False),
+        "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512),
+        "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512),
     }
     pre2 = torch.empty_like(preact) if k == "gradh" else None
     fl = kernel_flops(M, D, H, Dout)[{"gemm1": "gemm1_swiglu", "y": "gemm2_y", "dw2": "dw2_hprologue",

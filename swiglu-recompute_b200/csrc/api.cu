@@ -411,12 +411,15 @@ int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
 // the 2-SM (256-row tiles) kernel. p.tiles_n must be set; tiles_m is set here.
+// `tile_n` is the caller's preference for the pair tile's width (0 = the
+// 256-column default, 512 = 256 x 512 tiles); it applies where the size rule
+// picks the 2-SM kernel and no path is forced with swiglu_b200_set_gemm_path.
 template <bool A_MN, bool B_MN, int EPI, bool F32>
-int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
+int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) {
   const int tiles2 = ((p.M + 255) / 256) * p.tiles_n;
   int mode = g_gemm_path.load(std::memory_order_relaxed);
   // By size: pairs pay off once there is at least one full wave of them.
-  if (mode == 0) mode = tiles2 >= d.sms / 2 ? 2 : 1;
+  if (mode == 0) mode = tiles2 >= d.sms / 2 ? (tile_n == 512 ? 3 : 2) : 1;
   if (mode == 2 || mode == 3) {
     // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
     // fused_forward.py:58); a pair tile covers two of them.
@@ -527,7 +530,9 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
 }
 
 int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout, int b_layout,
-              int dtype, int out_dtype, int group_m, cudaStream_t st) {
+              int dtype, int out_dtype, int group_m, cudaStream_t st, int tile_n = 0) {
+  if (tile_n != 0 && tile_n != 256 && tile_n != 512)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "tile_n must be 0, 256 or 512");
   if (int rc = check_dims("matmul", M, N, K)) return rc;
   if (int rc = check_dtype(dtype)) return rc;
   if (int rc = check_dtype(out_dtype)) return rc;
@@ -582,7 +587,7 @@ int op_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64
   p.M = (int)M, p.N = (int)N, p.K = (int)K, p.H = 0, p.layout = 0;
   p.tiles_n = (int)((N + 255) / 256);
   p.group_m = group_m;
-#define SWIGLU_MM(AM, BM_, F) run_gemm<AM, BM_, kEpiStore, F>(p, *d, st)
+#define SWIGLU_MM(AM, BM_, F) run_gemm<AM, BM_, kEpiStore, F>(p, *d, st, tile_n)
   if (f32) {
     if (a_mn) return b_mn ? SWIGLU_MM(true, true, true) : SWIGLU_MM(true, false, true);
     return b_mn ? SWIGLU_MM(false, true, true) : SWIGLU_MM(false, false, true);
@@ -1002,6 +1007,12 @@ int swiglu_b200_matmul(const void* a, const void* b, void* c, int64_t M, int64_t
                    static_cast<cudaStream_t>(stream));
 }
 
+int swiglu_b200_matmul_tiled(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout,
+                             int b_layout, int dtype, int out_dtype, int group_size_m, int tile_n, void* stream) {
+  return op_matmul(a, b, c, M, N, K, a_layout, b_layout, dtype, out_dtype, group_size_m,
+                   static_cast<cudaStream_t>(stream), tile_n);
+}
+
 int swiglu_b200_bwd_dw2(const void* grad_y, const void* preact, void* dw2, int64_t M, int64_t H, int64_t Dout,
                         int dtype, int layout, void* stream) {
   return op_dw2(grad_y, preact, dw2, M, H, Dout, dtype, layout, static_cast<cudaStream_t>(stream));
@@ -1065,14 +1076,14 @@ int swiglu_b200_mlp_backward(const void* x, const void* w1, const void* w2, void
   }
   if (w_form == SWIGLU_W1_ROWS) {
     // grad_W1 [2H, D] = grad_preact^T . x (swiglu_recompute.py:76)
-    if (int rc = op_matmul(preact, x, dw1, 2 * H, D, M, 1, 0, dtype, dtype, 16, st)) return rc;
+    if (int rc = op_matmul(preact, x, dw1, 2 * H, D, M, 1, 0, dtype, dtype, 16, st, 512)) return rc;
     // grad_x [M, D] = grad_preact . W1, W1 stored [2H, D] (swiglu_recompute.py:77)
-    return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 0, dtype, dtype, 16, st);
+    return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 0, dtype, dtype, 16, st, 512);
   }
   // grad_wt [D, 2H] = x^T . grad_preact (fused_forward.py:282)
-  if (int rc = op_matmul(x, preact, dw1, D, 2 * H, M, 1, 0, dtype, dtype, 16, st)) return rc;
+  if (int rc = op_matmul(x, preact, dw1, D, 2 * H, M, 1, 0, dtype, dtype, 16, st, 512)) return rc;
   // grad_x [M, D] = grad_preact . wt^T, wt stored [D, 2H] (fused_forward.py:283)
-  return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 1, dtype, dtype, 16, st);
+  return op_matmul(preact, w1, dx, M, D, 2 * H, 0, 1, dtype, dtype, 16, st, 512);
 }
 
 }  // extern "C"

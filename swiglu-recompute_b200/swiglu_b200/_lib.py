@@ -34,6 +34,7 @@ _SIGNATURES = {
     "swiglu_b200_fused_matmul_swiglu_save_preact":
         [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
     "swiglu_b200_matmul": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
+    "swiglu_b200_matmul_tiled": [_p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i, _p],
     "swiglu_b200_matmul_scatter_rows":
         [_p, _p, _i64, _i64, _i64, _i, _i, _i, ctypes.POINTER(_p), _i, _i, _i64, _p],
     "swiglu_b200_tp_signal": [ctypes.POINTER(_p), _i, _i, ctypes.c_uint32, _p],

@@ -70,13 +70,13 @@ def _(x, w, w_form, layout, group_size_m):
 
 
 @torch.library.custom_op(f"{_NS}::matmul", mutates_args=(), device_types="cuda")
-def matmul(a: torch.Tensor, b: torch.Tensor, a_t: bool, b_t: bool) -> torch.Tensor:
-    """op(a) . op(b) in a's dtype."""
-    return ops.matmul(a, b, a_t=a_t, b_t=b_t)
+def matmul(a: torch.Tensor, b: torch.Tensor, a_t: bool, b_t: bool, tile_n: int) -> torch.Tensor:
+    """op(a) . op(b) in a's dtype (tile_n: preferred 2-SM tile width, 0 = default)."""
+    return ops.matmul(a, b, a_t=a_t, b_t=b_t, tile_n=tile_n)
 
 
 @matmul.register_fake
-def _(a, b, a_t, b_t):
+def _(a, b, a_t, b_t, tile_n):
     m = a.shape[1] if a_t else a.shape[0]
     n = b.shape[0] if b_t else b.shape[1]
     return a.new_empty((m, n))
@@ -124,8 +124,8 @@ class _Eager:
                               group_size_m=group_size_m)[0]
 
     @staticmethod
-    def matmul(a, b, a_t, b_t):
-        return ops.matmul(a, b, a_t=a_t, b_t=b_t)
+    def matmul(a, b, a_t, b_t, tile_n=0):
+        return ops.matmul(a, b, a_t=a_t, b_t=b_t, tile_n=tile_n)
 
     @staticmethod
     def bwd_dw2(grad_y, preact, layout):
@@ -152,8 +152,8 @@ class _Traced:
         return torch.ops.swiglu_b200.swiglu_fwd_preact(x, w, w_form, layout, group_size_m)
 
     @staticmethod
-    def matmul(a, b, a_t, b_t):
-        return torch.ops.swiglu_b200.matmul(a, b, a_t, b_t)
+    def matmul(a, b, a_t, b_t, tile_n=0):
+        return torch.ops.swiglu_b200.matmul(a, b, a_t, b_t, tile_n)
 
     @staticmethod
     def bwd_dw2(grad_y, preact, layout):

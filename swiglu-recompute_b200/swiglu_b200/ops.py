@@ -143,8 +143,9 @@ def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
 
 def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool, b_t: bool,
            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
-           group_size_m: int = DEFAULT_GROUP_M) -> torch.Tensor:
-    """C = op(a) . op(b); op(a) = a.T if a_t, op(b) = b.T if b_t."""
+           group_size_m: int = DEFAULT_GROUP_M, tile_n: int = 0) -> torch.Tensor:
+    """C = op(a) . op(b); op(a) = a.T if a_t, op(b) = b.T if b_t. tile_n = 512
+    asks the 2-SM kernel for 256 x 512 output tiles (long-K GEMMs)."""
     dev = _check_cuda(a, b, out)
     dt = _same_dtype(a, b)
     M, K = (a.shape[1], a.shape[0]) if a_t else tuple(a.shape)
@@ -156,8 +157,8 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool, b_t: bool,
     else:
         assert out.shape == (M, N) and out.dtype == odt
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_matmul", _p(a), _p(b), _p(out), M, N, K, int(a_t), int(b_t),
-                  dtype_code(dt), dtype_code(odt), int(group_size_m), _stream(dev))
+        _lib.call("swiglu_b200_matmul_tiled", _p(a), _p(b), _p(out), M, N, K, int(a_t), int(b_t),
+                  dtype_code(dt), dtype_code(odt), int(group_size_m), int(tile_n), _stream(dev))
     return out
 
 

@@ -101,13 +101,14 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
         if emit_h:
             grad_w2 = K.matmul(gy, h, True, False)                    # [Dout, H] = grad_y^T h
             del h
+        # dW1 and dx contract over the long M and 2H axes: 256 x 512 tiles.
         if need_w1:
             if w_form == W1_ROWS:
-                grad_w1 = K.matmul(gp, x, True, False)                # [2H, D] = gp^T x
+                grad_w1 = K.matmul(gp, x, True, False, 512)           # [2H, D] = gp^T x
             else:
-                grad_w1 = K.matmul(x, gp, True, False)                # [D, 2H] = x^T gp
+                grad_w1 = K.matmul(x, gp, True, False, 512)           # [D, 2H] = x^T gp
         if need_x:
-            grad_x = K.matmul(gp, w1, False, w_form != W1_ROWS)
+            grad_x = K.matmul(gp, w1, False, w_form != W1_ROWS, 512)
     return grad_x, grad_w1, grad_w2
 
 

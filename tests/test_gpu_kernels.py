@@ -176,3 +176,21 @@ def test_empty_batch_is_a_no_op_with_zero_weight_grads():
 
 def test_device_status_healthy_after_all_kernels():
     assert ops.device_status(0) == 0
+
+
+@pytest.mark.parametrize("a_t,b_t", [(True, False), (False, False), (False, True)])
+def test_matmul_tile_width_hint(a_t, b_t):
+    """tile_n=512 under the default path selection: a shape with more than a
+    wave of CTA pairs takes the 256 x 512 kernel; the result matches the
+    default tiles within the bf16 bound, and invalid widths are rejected."""
+    M, N, K = 2048, 3584, 1536
+    a = _r(*((K, M) if a_t else (M, K)), seed=21)
+    b = _r(*((N, K) if b_t else (K, N)), seed=22, scale=K ** -0.5)
+    ref = (a.float().t() if a_t else a.float()) @ (b.float().t() if b_t else b.float())
+    ad, bd = a.to(DEV), b.to(DEV)
+    wide = ops.matmul(ad, bd, a_t=a_t, b_t=b_t, tile_n=512)
+    narrow = ops.matmul(ad, bd, a_t=a_t, b_t=b_t)
+    assert O.rel_max(wide.cpu(), ref) <= BF16_TOL
+    assert O.rel_max(wide.cpu(), narrow.cpu().float()) <= BF16_TOL
+    with pytest.raises(_lib.SwigluError):
+        ops.matmul(ad, bd, a_t=a_t, b_t=b_t, tile_n=384)
