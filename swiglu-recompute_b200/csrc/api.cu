@@ -525,6 +525,17 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   p.flags = rounded ? kFlagHFromRounded : 0;
   if ((preact && reinterpret_cast<uintptr_t>(preact) % 16) || (h && reinterpret_cast<uintptr_t>(h) % 16))
     return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
+  // The 2-SM kernel stores preact and h with TMA when every 32-unit chunk
+  // below H is whole (its boxes are 32 columns wide).
+  if (H % 32 == 0) {
+    if (preact) {
+      if (int rc = make_store_map(&p.tmC, preact, 2 * H, M, 2 * H, false)) return rc;
+    }
+    if (h) {
+      if (int rc = make_store_map(&p.tmD, h, H, M, H, false)) return rc;
+    }
+    p.flags |= kFlagTmaEpilogue;
+  }
   return w_form == SWIGLU_W1_ROWS ? run_gemm<false, false, kEpiSwiglu, false>(p, *d, st)
                                   : run_gemm<false, true, kEpiSwiglu, false>(p, *d, st);
 }

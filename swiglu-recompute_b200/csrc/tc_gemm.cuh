@@ -55,7 +55,8 @@ __host__ __device__ __forceinline__ int gate_col(int j, int H, int layout) {
 struct TcParams {
   CUtensorMap tmA;  // A operand (box: K-major {64,128} / MN-major {64,64})
   CUtensorMap tmB;  // B operand (box: K-major {64,BN/2} / MN-major {64,64})
-  CUtensorMap tmC;  // output [M, N], {32 x 32} boxes: the TMA-store epilogue (2-SM kernel, kEpiStore)
+  CUtensorMap tmC;  // TMA-store epilogues (2-SM kernel), {32 x 32} boxes: store: D; swiglu: preact
+  CUtensorMap tmD;  // swiglu TMA-store epilogue: h
   void* out0;       // store: D; swiglu: preact; dswiglu: preact (in/out)
   void* out1;       // swiglu: h (may be null)
   long long ld0, ld1;
@@ -184,6 +185,7 @@ __device__ __noinline__ bool sk_publish_and_fix(uint32_t t_row, int ncols, float
 constexpr int kScatterStageFloats = 32 * 33;
 
 constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
+constexpr int kFlagTmaEpilogue = 2;   // swiglu: tmC / tmD are set and H % 32 == 0 (2-SM kernel)
 
 template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
 struct TcCfg {
@@ -304,6 +306,78 @@ __device__ __forceinline__ void epilogue_store_tma(const TcParams& p, int pn, in
     __syncwarp();
     if (lane == 0) {
       tma_store_2d(&p.tmC, buf, n0 + c * 32, row0);
+      bulk_commit();
+    }
+  }
+}
+
+// SwiGLU epilogue through shared memory and TMA (2-SM kernel; H % 32 == 0
+// so every 32-unit chunk below H is whole): per chunk of 32 hidden units a
+// warp fills up to three {32 x 32} bf16 boxes (preact left, preact gate, h;
+// 64-byte rows, 64-byte swizzle as in epilogue_store_tma) and one lane issues
+// their TMA stores. The single 6 KB staging area is reused once the previous
+// chunk's stores have read it. Chunks at or beyond H are skipped (in the
+// standard layout their left columns would fall on gate columns).
+struct SwigluStage {
+  static constexpr int kBoxBytes = 32 * 64;
+  static constexpr int kWarpBytes = 3 * kBoxBytes;
+};
+
+__device__ __forceinline__ void stage_row32_bf16(uint8_t* box, uint32_t lane, const float (&v)[32]) {
+  uint8_t* row = box + lane * 64;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint4 u = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                               pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+    *reinterpret_cast<uint4*>(row + 16 * (k ^ static_cast<int>((lane >> 1) & 3u))) = u;
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, int row0, uint32_t t_row,
+                                                    uint8_t* stage) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int j0 = pn * (BN / 2);
+  const bool rounded = (p.flags & kFlagHFromRounded) != 0;
+  uint8_t* lbox = stage;
+  uint8_t* gbox = stage + SwigluStage::kBoxBytes;
+  uint8_t* hbox = stage + 2 * SwigluStage::kBoxBytes;
+#pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    const int j = j0 + c * 32;
+    if (j >= p.H) break;
+    uint32_t rl[32], rg[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, rl);
+    tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
+    tmem_ld_wait();
+    float lf[32], gf[32], hf[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float l = __uint_as_float(rl[i]);
+      float g = __uint_as_float(rg[i]);
+      lf[i] = l;
+      gf[i] = g;
+      if (rounded) {
+        l = bf16_round(l);
+        g = bf16_round(g);
+      }
+      hf[i] = l * (g * sigmoid_fast(g));
+    }
+    if (lane == 0) bulk_wait_read<0>();  // the previous chunk's stores have read the boxes
+    __syncwarp();
+    if (p.out0) {
+      stage_row32_bf16(lbox, lane, lf);
+      stage_row32_bf16(gbox, lane, gf);
+    }
+    if (p.out1) stage_row32_bf16(hbox, lane, hf);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (p.out0) {
+        tma_store_2d(&p.tmC, lbox, left_col(j, p.H, p.layout), row0);
+        tma_store_2d(&p.tmC, gbox, gate_col(j, p.H, p.layout), row0);
+      }
+      if (p.out1) tma_store_2d(&p.tmD, hbox, j, row0);
       bulk_commit();
     }
   }

@@ -56,6 +56,7 @@ struct Tc2Cfg {
   static constexpr int EPI_STAGE_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
   static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4
                                          : EPI == kEpiStore     ? 4 * StoreStage<OUT_F32>::kWarpBytes
+                                         : EPI == kEpiSwiglu    ? 4 * SwigluStage::kWarpBytes
                                                                 : 0;
   static constexpr int SMEM_BYTES = 1024 + EPI_STAGE_OFFSET + EPI_STAGE_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -243,9 +244,16 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       float* stage = reinterpret_cast<float*>(smem + Cfg::EPI_STAGE_OFFSET) + (warp - 2) * kScatterStageFloats;
       uint8_t* store_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * StoreStage<Cfg::OUT_F32>::kWarpBytes;
       const int row0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32);
+      uint8_t* swiglu_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * SwigluStage::kWarpBytes;
       auto finish_tile = [&]() {
         if constexpr (Cfg::EPI == kEpiStore) {
           epilogue_store_tma<BN, Cfg::OUT_F32>(p, pn, row0, t_row, store_stage);
+        } else if constexpr (Cfg::EPI == kEpiSwiglu) {
+          if (p.flags & kFlagTmaEpilogue) {
+            epilogue_swiglu_tma<BN>(p, pn, row0, t_row, swiglu_stage);
+          } else {
+            epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+          }
         } else {
           epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
         }
@@ -271,7 +279,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       }
     }
     // The TMA stores read shared memory asynchronously: finish before exit.
-    if constexpr (Cfg::EPI == kEpiStore) {
+    if constexpr (Cfg::EPI == kEpiStore || Cfg::EPI == kEpiSwiglu) {
       if (lane == 0) bulk_wait_read<0>();
     }
   }
