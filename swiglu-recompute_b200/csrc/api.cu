@@ -418,6 +418,8 @@ template <bool A_MN, bool B_MN, int EPI, bool F32>
 int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) {
   const int tiles2 = ((p.M + 255) / 256) * p.tiles_n;
   int mode = g_gemm_path.load(std::memory_order_relaxed);
+  // The 2-SM dSwiGLU epilogue stores 32-column TMA boxes: whole chunks only.
+  if (EPI == kEpiDswiglu && !(p.flags & kFlagTmaEpilogue)) mode = 1;
   // By size: pairs pay off once there is at least one full wave of them.
   if (mode == 0) mode = tiles2 >= d.sms / 2 ? (tile_n == 512 ? 3 : 2) : 1;
   if (mode == 2 || mode == 3) {
@@ -804,6 +806,15 @@ int op_grad_preact(const void* gy, const void* w2, void* preact, void* h, int64_
   p.ld0 = 2 * H;
   p.out1 = h;
   p.ld1 = H;
+  // The 2-SM kernel stores grad_preact and h with TMA when every 32-unit
+  // chunk below H is whole (its boxes are 32 columns wide).
+  if (H % 32 == 0) {
+    if (int rc = make_store_map(&p.tmC, preact, 2 * H, M, 2 * H, false)) return rc;
+    if (h) {
+      if (int rc = make_store_map(&p.tmD, h, H, M, H, false)) return rc;
+    }
+    p.flags |= kFlagTmaEpilogue;
+  }
   p.M = (int)M, p.N = (int)H, p.K = (int)Dout, p.H = (int)H, p.layout = layout;
   p.tiles_n = (int)((H + 255) / 256);
   p.group_m = 16;

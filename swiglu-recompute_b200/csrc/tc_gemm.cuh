@@ -185,7 +185,7 @@ __device__ __noinline__ bool sk_publish_and_fix(uint32_t t_row, int ncols, float
 constexpr int kScatterStageFloats = 32 * 33;
 
 constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
-constexpr int kFlagTmaEpilogue = 2;   // swiglu: tmC / tmD are set and H % 32 == 0 (2-SM kernel)
+constexpr int kFlagTmaEpilogue = 2;   // swiglu / dswiglu: tmC / tmD are set and H % 32 == 0 (2-SM kernel)
 
 template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
 struct TcCfg {
@@ -379,6 +379,96 @@ __device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, i
       }
       if (p.out1) tma_store_2d(&p.tmD, hbox, j, row0);
       bulk_commit();
+    }
+  }
+}
+
+// dSwiGLU epilogue with TMA stores (the 2-SM kernel's only dSwiGLU epilogue;
+// it needs H % 32 == 0): preact left/gate are read per lane with the next
+// chunk prefetched into registers, and grad_left, grad_gate (over preact, in
+// place) and h leave through three {32 x 32} swizzled shared-memory boxes and
+// TMA stores, which takes the per-lane store traffic off the SM's L1 path.
+template <int BN>
+__device__ __forceinline__ void epilogue_dswiglu_tma(const TcParams& p, int pn, int row, int row0, uint32_t t_row,
+                                                     uint8_t* stage) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const bool row_ok = row < p.M;
+  const int j0 = pn * BN;
+  const __nv_bfloat16* pre_row =
+      reinterpret_cast<const __nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
+  uint8_t* lbox = stage;
+  uint8_t* gbox = stage + SwigluStage::kBoxBytes;
+  uint8_t* hbox = stage + 2 * SwigluStage::kBoxBytes;
+  const int swz = static_cast<int>((lane >> 1) & 3u);
+  // preact left/gate of the current chunk and, loaded one chunk ahead, the next.
+  uint4 lcur[4], gcur[4], lnext[4], gnext[4];
+  auto load_chunk = [&](int c, uint4 (&lu)[4], uint4 (&gu)[4]) {
+    const int j = j0 + c * 32;
+    const int lc = left_col(j, p.H, p.layout);
+    const int gc = gate_col(j, p.H, p.layout);
+    const bool ok = row_ok && j < p.N;  // whole chunks: H % 32 == 0
+#pragma unroll
+    for (int v8 = 0; v8 < 4; ++v8) {
+      lu[v8] = ok ? *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8) : make_uint4(0, 0, 0, 0);
+      gu[v8] = ok ? *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load_chunk(0, lcur, gcur);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int j = j0 + c * 32;
+    if (j >= p.N) break;
+    if (c + 1 < BN / 32) load_chunk(c + 1, lnext, gnext);
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    tmem_ld_wait();
+    if (lane == 0) bulk_wait_read<0>();  // the previous chunk's stores have read the boxes
+    __syncwarp();
+#pragma unroll
+    for (int v8 = 0; v8 < 4; ++v8) {
+      const uint32_t lw[4] = {lcur[v8].x, lcur[v8].y, lcur[v8].z, lcur[v8].w};
+      const uint32_t gw[4] = {gcur[v8].x, gcur[v8].y, gcur[v8].z, gcur[v8].w};
+      uint32_t glw[4], ggw[4], hw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 l2 = unpack_bf16x2(lw[e]);
+        const float2 g2 = unpack_bf16x2(gw[e]);
+        const float ls[2] = {l2.x, l2.y};
+        const float gs[2] = {g2.x, g2.y};
+        float glv[2], ggv[2], hv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = 8 * v8 + 2 * e + u;
+          // grad_h is a bf16 tensor in the reference before the pointwise step.
+          const float dh = bf16_round(__uint_as_float(r[i]));
+          const float sg = sigmoid_fast(gs[u]);
+          const float silu = gs[u] * sg;
+          const float dsilu = sg + silu * (1.0f - sg);
+          glv[u] = dh * silu;
+          ggv[u] = dh * ls[u] * dsilu;
+          hv[u] = ls[u] * silu;  // the dW2 prologue's h, bit for bit
+        }
+        glw[e] = pack_bf16x2(glv[0], glv[1]);
+        ggw[e] = pack_bf16x2(ggv[0], ggv[1]);
+        hw[e] = pack_bf16x2(hv[0], hv[1]);
+      }
+      const int off = static_cast<int>(lane) * 64 + 16 * (v8 ^ swz);
+      *reinterpret_cast<uint4*>(lbox + off) = make_uint4(glw[0], glw[1], glw[2], glw[3]);
+      *reinterpret_cast<uint4*>(gbox + off) = make_uint4(ggw[0], ggw[1], ggw[2], ggw[3]);
+      if (p.out1) *reinterpret_cast<uint4*>(hbox + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&p.tmC, lbox, left_col(j, p.H, p.layout), row0);
+      tma_store_2d(&p.tmC, gbox, gate_col(j, p.H, p.layout), row0);
+      if (p.out1) tma_store_2d(&p.tmD, hbox, j, row0);
+      bulk_commit();
+    }
+#pragma unroll
+    for (int v8 = 0; v8 < 4; ++v8) {
+      lcur[v8] = lnext[v8];
+      gcur[v8] = gnext[v8];
     }
   }
 }

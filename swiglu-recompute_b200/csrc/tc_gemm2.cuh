@@ -56,8 +56,8 @@ struct Tc2Cfg {
   static constexpr int EPI_STAGE_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
   static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4
                                          : EPI == kEpiStore     ? 4 * StoreStage<OUT_F32>::kWarpBytes
-                                         : EPI == kEpiSwiglu    ? 4 * SwigluStage::kWarpBytes
-                                                                : 0;
+                                         : EPI == kEpiSwiglu || EPI == kEpiDswiglu ? 4 * SwigluStage::kWarpBytes
+                                                                                   : 0;
   static constexpr int SMEM_BYTES = 1024 + EPI_STAGE_OFFSET + EPI_STAGE_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
           } else {
             epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
           }
+        } else if constexpr (Cfg::EPI == kEpiDswiglu) {
+          epilogue_dswiglu_tma<BN>(p, pn, row, row0, t_row, swiglu_stage);  // host ensures H % 32 == 0
         } else {
           epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
         }
@@ -279,7 +281,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       }
     }
     // The TMA stores read shared memory asynchronously: finish before exit.
-    if constexpr (Cfg::EPI == kEpiStore || Cfg::EPI == kEpiSwiglu) {
+    if constexpr (Cfg::EPI == kEpiStore || Cfg::EPI == kEpiSwiglu || Cfg::EPI == kEpiDswiglu) {
       if (lane == 0) bulk_wait_read<0>();
     }
   }
