@@ -125,15 +125,12 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
 #pragma unroll
         for (int sub = 0; sub < Cfg::NSUB; ++sub) {
           if constexpr (Cfg::EPI == kEpiSwiglu) {
-            // Accumulator columns [0, BN/2) are left units, [BN/2, BN) gate
-            // units of the tile's BN/2 hidden units j0...
-            const int j0 = pn * (BN / 2);
-            if constexpr (Cfg::NSUB == 1) {  // ...rank 0 holds the left half, rank 1 the gate half
-              b0[sub] = leader ? left_col(j0, p.H, p.layout) : gate_col(j0, p.H, p.layout);
-            } else {  // ...MMA 0 the left units, MMA 1 the gate units, split by rank
-              const int j = j0 + 128 * static_cast<int>(rank);
-              b0[sub] = sub == 0 ? left_col(j, p.H, p.layout) : gate_col(j, p.H, p.layout);
-            }
+            const int j0 = pn * (BN / 2);  // the tile's BN/2 hidden units start at j0
+            // MMA `sub` covers units j0 + 128 sub .. + 127: rank 0 holds their
+            // left columns, rank 1 their gate columns, so each 256-column half
+            // of the accumulator is [left 128 | gate 128] and drains on its own.
+            const int j = j0 + 128 * sub;
+            b0[sub] = leader ? left_col(j, p.H, p.layout) : gate_col(j, p.H, p.layout);
           } else {
             b0[sub] = pn * BN + 256 * sub + 128 * static_cast<int>(rank);
           }
@@ -185,33 +182,71 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       constexpr uint32_t idesc = make_idesc_f16(256, 256, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
+      // The MMAs of one k-block of one 256-column accumulator half.
+      auto issue_sub = [&](uint32_t st, int sub, uint32_t d_tmem, bool first_kb) {
+        const uint32_t sa = smem_u32(smem + st * Cfg::STAGE_BYTES);
+        const uint32_t sbs = sa + Cfg::A_BYTES + sub * Cfg::SUB_B_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
+                                           : make_smem_desc_sw128(sa + k * 32, 16, 1024);
+          const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sbs + k * 2048, p.mn_lbo, p.mn_sbo)
+                                           : make_smem_desc_sw128(sbs + k * 32, 16, 1024);
+          umma_f16_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (!first_kb || k != 0) ? 1u : 0u);
+        }
+      };
+      auto release = [&](uint32_t st) {
+        umma_commit_pair(map_to_rank(&empty[st], 0));
+        umma_commit_pair(map_to_rank(&empty[st], 1));
+      };
       for (int u = first_unit; u < num_units && ok; u += unit_step) {
         const SkUnit w = sk_unit(p, u, num_kb);
-        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
-        tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        int kb = w.kb0;
+        if constexpr (Cfg::NSUB == 2) {
+          // One accumulator fills TMEM, but the epilogue frees its halves one
+          // after the other (tmem_empty[0], then [1]): start this tile on half
+          // 0 for up to a ring's worth of k-blocks while half 1 still drains,
+          // then back-fill half 1 for those k-blocks and release their stages.
+          // Each half still accumulates its k-blocks in order.
+          if (!mbar_wait(&tmem_empty[0], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+          tc_fence_after_sync();
+          const int ahead = min(STAGES, w.kb1 - w.kb0);
+          const uint32_t stage0 = stage;
+          for (int i = 0; i < ahead; ++i) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after_sync();
+            issue_sub(stage, 0, d_tmem, i == 0);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          if (!mbar_wait(&tmem_empty[1], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+          tc_fence_after_sync();
+          for (int i = 0; i < ahead; ++i) {
+            const uint32_t st = (stage0 + i) % STAGES;
+            issue_sub(st, 1, d_tmem, i == 0);
+            release(st);
+          }
+          kb += ahead;
+        } else {
+          if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, status, kErrTimeoutMma)) break;
+          tc_fence_after_sync();
+        }
+        for (; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, status, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-          const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
-                                             : make_smem_desc_sw128(sa + k * 32, 16, 1024);
-#pragma unroll
-            for (int sub = 0; sub < Cfg::NSUB; ++sub) {
-              const uint32_t sbs = sb + sub * Cfg::SUB_B_BYTES;
-              const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sbs + k * 2048, p.mn_lbo, p.mn_sbo)
-                                               : make_smem_desc_sw128(sbs + k * 32, 16, 1024);
-              umma_f16_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
-            }
-          }
-          umma_commit_pair(map_to_rank(&empty[stage], 0));
-          umma_commit_pair(map_to_rank(&empty[stage], 1));
+          for (int sub = 0; sub < Cfg::NSUB; ++sub) issue_sub(stage, sub, d_tmem, kb == w.kb0);
+          release(stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -245,23 +280,37 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       uint8_t* store_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * StoreStage<Cfg::OUT_F32>::kWarpBytes;
       const int row0 = pm * Cfg::BM + Cfg::BMH * static_cast<int>(rank) + static_cast<int>(q * 32);
       uint8_t* swiglu_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * SwigluStage::kWarpBytes;
-      auto finish_tile = [&]() {
+      // Epilogue of accumulator half `sub` (256 columns): a 256-column tile
+      // of its own, column block pn * NSUB + sub.
+      auto finish_sub = [&](int sub) {
+        const int pns = pn * Cfg::NSUB + sub;
+        const uint32_t ts = t_row + 256 * sub;
         if constexpr (Cfg::EPI == kEpiStore) {
-          epilogue_store_tma<BN, Cfg::OUT_F32>(p, pn, row0, t_row, store_stage);
+          epilogue_store_tma<256, Cfg::OUT_F32>(p, pns, row0, ts, store_stage);
         } else if constexpr (Cfg::EPI == kEpiSwiglu) {
           if (p.flags & kFlagTmaEpilogue) {
-            epilogue_swiglu_tma<BN>(p, pn, row0, t_row, swiglu_stage);
+            epilogue_swiglu_tma<256>(p, pns, row0, ts, swiglu_stage);
           } else {
-            epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+            epilogue_tile<256, Cfg::EPI, Cfg::OUT_F32>(p, pm, pns, row, ts, stage);
           }
         } else if constexpr (Cfg::EPI == kEpiDswiglu) {
-          epilogue_dswiglu_tma<BN>(p, pn, row, row0, t_row, swiglu_stage);  // host ensures H % 32 == 0
+          epilogue_dswiglu_tma<256>(p, pns, row, row0, ts, swiglu_stage);  // host ensures H % 32 == 0
         } else {
-          epilogue_tile<BN, Cfg::EPI, Cfg::OUT_F32>(p, pm, pn, row, t_row, stage);
+          epilogue_tile<256, Cfg::EPI, Cfg::OUT_F32>(p, pm, pns, row, ts, stage);
         }
       };
+      // Frees accumulator half `sub` (NSUB == 2) or the whole buffer.
+      auto free_acc = [&](int sub) {
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[Cfg::NSUB == 2 ? sub : acc], 0));
+      };
       if (w.parts == 1) {
-        finish_tile();
+#pragma unroll 1
+        for (int sub = 0; sub < Cfg::NSUB; ++sub) {
+          finish_sub(sub);
+          free_acc(sub);
+        }
       } else {
         // Stream-K part: the last of the parts to arrive for this 32-row
         // slab finishes the tile.
@@ -269,12 +318,11 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         const long long part_stride = static_cast<long long>(Cfg::BM) * BN;
         const float* fix = p.sk_partials + (static_cast<long long>(i) * w.parts * Cfg::BM + row_in_tile) * BN;
         if (sk_publish_and_fix(t_row, BN, const_cast<float*>(fix) + w.part * part_stride, fix, part_stride, w.parts,
-                               p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch))
-          finish_tile();
+                               p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch)) {
+          for (int sub = 0; sub < Cfg::NSUB; ++sub) finish_sub(sub);
+        }
+        for (int sub = 0; sub < Cfg::NSUB; ++sub) free_acc(sub);
       }
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(map_to_rank(&tmem_empty[acc], 0));
       if (++acc == Cfg::ACCS) {
         acc = 0;
         acc_phase ^= 1;
