@@ -359,7 +359,10 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e
         # End to end with host buffers: this rank's token shard in from pinned
         # host memory and its grad_x out, on a copy stream one step ahead of
         # the compute (the single-GPU bench's pipelined loop), max over ranks.
-        e2e_ms, h2d, d2h = e2e_fn(model, params, x_l.cpu(), gy_l.cpu(), dev, args)
+        x_host, gy_host = x_l.cpu(), gy_l.cpu()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2e_ms, h2d, d2h = e2e_fn(model, params, x_host, gy_host, dev, args)
         e2e_ms = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
         e2e_ms = e2e_ms.item()
