@@ -383,51 +383,59 @@ __device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, i
   }
 }
 
-// dSwiGLU epilogue with TMA stores (the 2-SM kernel's only dSwiGLU epilogue;
-// it needs H % 32 == 0): preact left/gate are read per lane with the next
-// chunk prefetched into registers, and grad_left, grad_gate (over preact, in
-// place) and h leave through three {32 x 32} swizzled shared-memory boxes and
-// TMA stores, which takes the per-lane store traffic off the SM's L1 path.
+// dSwiGLU epilogue of the 2-SM kernel (needs H % 32 == 0), all through TMA:
+// per chunk of 32 hidden units a warp TMA-loads the preact left and gate
+// {32 x 32} boxes of its 32 rows into one of two buffers (the next chunk's
+// load is in flight while this one is computed), each thread reads its row,
+// writes grad_left / grad_gate back into the same boxes and h into a third,
+// and one lane TMA-stores the three (grad_preact over preact, in place). No
+// per-lane global loads or stores remain. Box rows are 64 bytes with the
+// 64-byte swizzle of epilogue_store_tma. `lbar` holds this warp's two
+// load barriers; `lphase` their parities, kept across tiles.
+struct DswigluStage {
+  static constexpr int kBoxBytes = 32 * 64;
+  static constexpr int kBufBytes = 3 * kBoxBytes;  // left, gate, h
+  static constexpr int kWarpBytes = 2 * kBufBytes;
+};
+
 template <int BN>
-__device__ __forceinline__ void epilogue_dswiglu_tma(const TcParams& p, int pn, int row, int row0, uint32_t t_row,
-                                                     uint8_t* stage) {
+__device__ __forceinline__ bool epilogue_dswiglu_tma(const TcParams& p, int pn, int row0, uint32_t t_row,
+                                                     uint8_t* stage, uint64_t* lbar, uint32_t& lphase,
+                                                     volatile int* abort_flag) {
   const uint32_t lane = threadIdx.x & 31u;
-  const bool row_ok = row < p.M;
   const int j0 = pn * BN;
-  const __nv_bfloat16* pre_row =
-      reinterpret_cast<const __nv_bfloat16*>(p.out0) + static_cast<long long>(row) * p.ld0;
-  uint8_t* lbox = stage;
-  uint8_t* gbox = stage + SwigluStage::kBoxBytes;
-  uint8_t* hbox = stage + 2 * SwigluStage::kBoxBytes;
+  int nch = 0;  // whole chunks below N
+  while (nch < BN / 32 && j0 + 32 * nch < p.N) ++nch;
   const int swz = static_cast<int>((lane >> 1) & 3u);
-  // preact left/gate of the current chunk and, loaded one chunk ahead, the next.
-  uint4 lcur[4], gcur[4], lnext[4], gnext[4];
-  auto load_chunk = [&](int c, uint4 (&lu)[4], uint4 (&gu)[4]) {
-    const int j = j0 + c * 32;
-    const int lc = left_col(j, p.H, p.layout);
-    const int gc = gate_col(j, p.H, p.layout);
-    const bool ok = row_ok && j < p.N;  // whole chunks: H % 32 == 0
-#pragma unroll
-    for (int v8 = 0; v8 < 4; ++v8) {
-      lu[v8] = ok ? *reinterpret_cast<const uint4*>(pre_row + lc + 8 * v8) : make_uint4(0, 0, 0, 0);
-      gu[v8] = ok ? *reinterpret_cast<const uint4*>(pre_row + gc + 8 * v8) : make_uint4(0, 0, 0, 0);
-    }
+  auto issue_load = [&](int c) {  // lane 0; the buffer's earlier stores must have read it
+    uint8_t* buf = stage + (c & 1) * DswigluStage::kBufBytes;
+    const int j = j0 + 32 * c;
+    bulk_wait_read<0>();
+    mbar_arrive_expect_tx(&lbar[c & 1], 2 * DswigluStage::kBoxBytes);
+    tma_load_2d(buf, &p.tmC, &lbar[c & 1], left_col(j, p.H, p.layout), row0);
+    tma_load_2d(buf + DswigluStage::kBoxBytes, &p.tmC, &lbar[c & 1], gate_col(j, p.H, p.layout), row0);
   };
-  load_chunk(0, lcur, gcur);
+  if (nch > 0 && lane == 0) issue_load(0);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    const int j = j0 + c * 32;
-    if (j >= p.N) break;
-    if (c + 1 < BN / 32) load_chunk(c + 1, lnext, gnext);
+  for (int c = 0; c < nch; ++c) {
+    const int j = j0 + 32 * c;
+    if (c + 1 < nch && lane == 0) issue_load(c + 1);
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c * 32, r);
     tmem_ld_wait();
-    if (lane == 0) bulk_wait_read<0>();  // the previous chunk's stores have read the boxes
-    __syncwarp();
+    const uint32_t b = static_cast<uint32_t>(c & 1);
+    if (!mbar_wait(&lbar[b], (lphase >> b) & 1u, abort_flag, p.status, kErrTimeoutEpilogue)) return false;
+    lphase ^= 1u << b;
+    uint8_t* lbox = stage + b * DswigluStage::kBufBytes;
+    uint8_t* gbox = lbox + DswigluStage::kBoxBytes;
+    uint8_t* hbox = gbox + DswigluStage::kBoxBytes;
 #pragma unroll
     for (int v8 = 0; v8 < 4; ++v8) {
-      const uint32_t lw[4] = {lcur[v8].x, lcur[v8].y, lcur[v8].z, lcur[v8].w};
-      const uint32_t gw[4] = {gcur[v8].x, gcur[v8].y, gcur[v8].z, gcur[v8].w};
+      const int off = static_cast<int>(lane) * 64 + 16 * (v8 ^ swz);
+      const uint4 lu = *reinterpret_cast<const uint4*>(lbox + off);
+      const uint4 gu = *reinterpret_cast<const uint4*>(gbox + off);
+      const uint32_t lw[4] = {lu.x, lu.y, lu.z, lu.w};
+      const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
       uint32_t glw[4], ggw[4], hw[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -452,7 +460,6 @@ __device__ __forceinline__ void epilogue_dswiglu_tma(const TcParams& p, int pn, 
         ggw[e] = pack_bf16x2(ggv[0], ggv[1]);
         hw[e] = pack_bf16x2(hv[0], hv[1]);
       }
-      const int off = static_cast<int>(lane) * 64 + 16 * (v8 ^ swz);
       *reinterpret_cast<uint4*>(lbox + off) = make_uint4(glw[0], glw[1], glw[2], glw[3]);
       *reinterpret_cast<uint4*>(gbox + off) = make_uint4(ggw[0], ggw[1], ggw[2], ggw[3]);
       if (p.out1) *reinterpret_cast<uint4*>(hbox + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -465,12 +472,8 @@ __device__ __forceinline__ void epilogue_dswiglu_tma(const TcParams& p, int pn, 
       if (p.out1) tma_store_2d(&p.tmD, hbox, j, row0);
       bulk_commit();
     }
-#pragma unroll
-    for (int v8 = 0; v8 < 4; ++v8) {
-      lcur[v8] = lnext[v8];
-      gcur[v8] = gnext[v8];
-    }
   }
+  return true;
 }
 
 template <int BN, int EPI, bool OUT_F32>

@@ -48,7 +48,9 @@ struct Tc2Cfg {
   static constexpr int SUB_B_BYTES = 128 * BK * 2;     // 16 KB: this CTA's half of one N=256 MMA's B
   static constexpr int B_BYTES = NSUB * SUB_B_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = NSUB == 1 ? 6 : 4;
+  // The dSwiGLU epilogue stages preact, grad and h boxes (48 KB), one ring
+  // stage's worth of shared memory.
+  static constexpr int STAGES = (NSUB == 1 ? 6 : 4) - (EPI_ == kEpiDswiglu ? 1 : 0);
   static constexpr int ACCS = NSUB == 1 ? 2 : 1;       // accumulator buffers in TMEM
   static constexpr int TMEM_COLS = 512;
   static constexpr int NUM_THREADS = 192;
@@ -56,8 +58,9 @@ struct Tc2Cfg {
   static constexpr int EPI_STAGE_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
   static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4
                                          : EPI == kEpiStore     ? 4 * StoreStage<OUT_F32>::kWarpBytes
-                                         : EPI == kEpiSwiglu || EPI == kEpiDswiglu ? 4 * SwigluStage::kWarpBytes
-                                                                                   : 0;
+                                         : EPI == kEpiSwiglu    ? 4 * SwigluStage::kWarpBytes
+                                         : EPI == kEpiDswiglu   ? 4 * DswigluStage::kWarpBytes + 64
+                                                                : 0;
   static constexpr int SMEM_BYTES = 1024 + EPI_STAGE_OFFSET + EPI_STAGE_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -90,6 +93,10 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       mbar_init(&tmem_empty[a], 8);
     }
     mbar_init(mma_done, 1);
+    if constexpr (Cfg::EPI == kEpiDswiglu) {
+      uint64_t* lb = reinterpret_cast<uint64_t*>(smem + Cfg::EPI_STAGE_OFFSET + 4 * DswigluStage::kWarpBytes);
+      for (int i = 0; i < 8; ++i) mbar_init(&lb[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -267,7 +274,12 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
   } else {
     const uint32_t q = warp & 3u;
     uint32_t acc = 0, acc_phase = 0;
-    for (int u = first_unit; u < num_units; u += unit_step) {
+    uint32_t dsw_phase = 0;  // parities of this warp's two preact-load barriers (dSwiGLU)
+    uint8_t* dsw_stage = smem + Cfg::EPI_STAGE_OFFSET + (warp - 2) * DswigluStage::kWarpBytes;
+    uint64_t* dsw_bar =
+        reinterpret_cast<uint64_t*>(smem + Cfg::EPI_STAGE_OFFSET + 4 * DswigluStage::kWarpBytes) + 2 * (warp - 2);
+    bool epi_ok = true;
+    for (int u = first_unit; u < num_units && epi_ok; u += unit_step) {
       const SkUnit w = sk_unit(p, u, num_kb);
       int pm, pn;
       tile_coords(w.tile, p.tiles_m, p.tiles_n, p.group_m, pm, pn);
@@ -294,7 +306,8 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
             epilogue_tile<256, Cfg::EPI, Cfg::OUT_F32>(p, pm, pns, row, ts, stage);
           }
         } else if constexpr (Cfg::EPI == kEpiDswiglu) {
-          epilogue_dswiglu_tma<256>(p, pns, row, row0, ts, swiglu_stage);  // host ensures H % 32 == 0
+          // host ensures H % 32 == 0
+          epi_ok = epi_ok && epilogue_dswiglu_tma<256>(p, pns, row0, ts, dsw_stage, dsw_bar, dsw_phase, abort_flag);
         } else {
           epilogue_tile<256, Cfg::EPI, Cfg::OUT_F32>(p, pm, pns, row, ts, stage);
         }
