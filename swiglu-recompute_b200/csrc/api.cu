@@ -434,7 +434,8 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) 
     return launch_tc2<Tc2Cfg<A_MN, B_MN, EPI, F32>>(p, d, st);
   }
   p.tiles_m = (p.M + 127) / 128;
-  return launch_tc<TcCfg<256, A_MN, B_MN, EPI, F32>>(p, d, st);
+  // The single-SM kernel has the per-lane SwiGLU epilogue only.
+  return launch_tc<TcCfg<256, A_MN, B_MN, EPI == kEpiSwigluTma ? kEpiSwiglu : EPI, F32>>(p, d, st);
 }
 
 template <bool A_MN, bool B_MN, int EPI, bool TRANSFORM>
@@ -528,15 +529,18 @@ int op_swiglu_fwd(const void* x, const void* w, void* preact, void* h, int64_t M
   if ((preact && reinterpret_cast<uintptr_t>(preact) % 16) || (h && reinterpret_cast<uintptr_t>(h) % 16))
     return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
   // The 2-SM kernel stores preact and h with TMA when every 32-unit chunk
-  // below H is whole (its boxes are 32 columns wide).
-  if (H % 32 == 0) {
+  // below H is whole (its boxes are 32 columns wide) and M >= 4096: measured
+  // on B200 at K=4096 H=14336, TMA stores take M=4096 from 0.668 to 0.653 ms
+  // and config 2 from 1.604 to 1.569 ms, but M=1024 from 0.204 to 0.224 ms.
+  if (H % 32 == 0 && M >= 4096) {
     if (preact) {
       if (int rc = make_store_map(&p.tmC, preact, 2 * H, M, 2 * H, false)) return rc;
     }
     if (h) {
       if (int rc = make_store_map(&p.tmD, h, H, M, H, false)) return rc;
     }
-    p.flags |= kFlagTmaEpilogue;
+    return w_form == SWIGLU_W1_ROWS ? run_gemm<false, false, kEpiSwigluTma, false>(p, *d, st)
+                                    : run_gemm<false, true, kEpiSwigluTma, false>(p, *d, st);
   }
   return w_form == SWIGLU_W1_ROWS ? run_gemm<false, false, kEpiSwiglu, false>(p, *d, st)
                                   : run_gemm<false, true, kEpiSwiglu, false>(p, *d, st);

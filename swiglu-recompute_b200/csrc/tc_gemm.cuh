@@ -37,7 +37,12 @@
 
 namespace swiglu {
 
-enum EpiKind : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiDswiglu = 2, kEpiScatterRows = 3 };
+enum EpiKind : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiDswiglu = 2, kEpiScatterRows = 3, kEpiSwigluTma = 4 };
+// kEpiSwigluTma: the SwiGLU epilogue storing through shared memory and TMA
+// (2-SM kernel only). A kind of its own so that the per-lane SwiGLU kernel
+// does not reserve the staging buffers: shared memory taken from the
+// unified L1 slowed that kernel by 10 % at M = 1024.
+__host__ __device__ constexpr bool is_swiglu(int epi) { return epi == kEpiSwiglu || epi == kEpiSwigluTma; }
 enum Layout : int { kLayoutStd = 0, kLayoutPacked = 1 };
 
 constexpr int kPackChunk = 128;  // BLOCK_SIZE_N_HALF of the packed layout (fused_forward_packed.py:41)
@@ -185,7 +190,7 @@ __device__ __noinline__ bool sk_publish_and_fix(uint32_t t_row, int ncols, float
 constexpr int kScatterStageFloats = 32 * 33;
 
 constexpr int kFlagHFromRounded = 1;  // h computed from the bf16-rounded preact
-constexpr int kFlagTmaEpilogue = 2;   // swiglu / dswiglu: tmC / tmD are set and H % 32 == 0 (2-SM kernel)
+constexpr int kFlagTmaEpilogue = 2;   // dswiglu: tmC / tmD are set and H % 32 == 0 (2-SM kernel)
 
 template <int BN_, bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_>
 struct TcCfg {

@@ -58,7 +58,7 @@ struct Tc2Cfg {
   static constexpr int EPI_STAGE_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
   static constexpr int EPI_STAGE_BYTES = EPI == kEpiScatterRows ? 4 * kScatterStageFloats * 4
                                          : EPI == kEpiStore     ? 4 * StoreStage<OUT_F32>::kWarpBytes
-                                         : EPI == kEpiSwiglu    ? 4 * SwigluStage::kWarpBytes
+                                         : EPI == kEpiSwigluTma ? 4 * SwigluStage::kWarpBytes
                                          : EPI == kEpiDswiglu   ? 4 * DswigluStage::kWarpBytes + 64
                                                                 : 0;
   static constexpr int SMEM_BYTES = 1024 + EPI_STAGE_OFFSET + EPI_STAGE_BYTES;
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         int b0[Cfg::NSUB];
 #pragma unroll
         for (int sub = 0; sub < Cfg::NSUB; ++sub) {
-          if constexpr (Cfg::EPI == kEpiSwiglu) {
+          if constexpr (is_swiglu(Cfg::EPI)) {
             const int j0 = pn * (BN / 2);  // the tile's BN/2 hidden units start at j0
             // MMA `sub` covers units j0 + 128 sub .. + 127: rank 0 holds their
             // left columns, rank 1 their gate columns, so each 256-column half
@@ -299,12 +299,8 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         const uint32_t ts = t_row + 256 * sub;
         if constexpr (Cfg::EPI == kEpiStore) {
           epilogue_store_tma<256, Cfg::OUT_F32>(p, pns, row0, ts, store_stage);
-        } else if constexpr (Cfg::EPI == kEpiSwiglu) {
-          if (p.flags & kFlagTmaEpilogue) {
-            epilogue_swiglu_tma<256>(p, pns, row0, ts, swiglu_stage);
-          } else {
-            epilogue_tile<256, Cfg::EPI, Cfg::OUT_F32>(p, pm, pns, row, ts, stage);
-          }
+        } else if constexpr (Cfg::EPI == kEpiSwigluTma) {
+          epilogue_swiglu_tma<256>(p, pns, row0, ts, swiglu_stage);
         } else if constexpr (Cfg::EPI == kEpiDswiglu) {
           // host ensures H % 32 == 0
           epi_ok = epi_ok && epilogue_dswiglu_tma<256>(p, pns, row0, ts, dsw_stage, dsw_bar, dsw_phase, abort_flag);
@@ -342,7 +338,7 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
       }
     }
     // The TMA stores read shared memory asynchronously: finish before exit.
-    if constexpr (Cfg::EPI == kEpiStore || Cfg::EPI == kEpiSwiglu || Cfg::EPI == kEpiDswiglu) {
+    if constexpr (Cfg::EPI == kEpiStore || Cfg::EPI == kEpiSwigluTma || Cfg::EPI == kEpiDswiglu) {
       if (lane == 0) bulk_wait_read<0>();
     }
   }

@@ -194,3 +194,35 @@ def test_matmul_tile_width_hint(a_t, b_t):
     assert O.rel_max(wide.cpu(), narrow.cpu().float()) <= BF16_TOL
     with pytest.raises(_lib.SwigluError):
         ops.matmul(ad, bd, a_t=a_t, b_t=b_t, tile_n=384)
+
+
+@pytest.mark.parametrize("path", [2, 3], ids=["n256", "n512"])
+@pytest.mark.parametrize("form,layout", [(ops.W1_ROWS, O.STD), (ops.W1_T, O.PACKED)])
+@pytest.mark.parametrize("want_preact", [True, False])
+def test_swiglu_forward_tma_epilogue(path, form, layout, want_preact):
+    """M >= 4096 with H % 32 == 0 takes the 2-SM kernel's TMA-store SwiGLU
+    epilogue (preact and h staged in shared memory); checked against the
+    oracle, and the h-only form against the full one bit for bit."""
+    M, K, H = 4096, 256, 640
+    x = _r(M, K, seed=31)
+    w_rows_std = _r(2 * H, K, seed=32, scale=K ** -0.5)
+    li, gi = O.col_index(H, layout)
+    w_rows = torch.empty_like(w_rows_std)
+    w_rows[li] = w_rows_std[:H]
+    w_rows[gi] = w_rows_std[H:]
+    w = (w_rows if form == ops.W1_ROWS else w_rows.t().contiguous()).to(DEV)
+    lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
+    _lib.set_gemm_path(path)
+    try:
+        full_pre, full_h = ops.swiglu_fwd(x.to(DEV), w, w_form=form, layout=lay, h_from_rounded=True)
+        pre, h = ops.swiglu_fwd(x.to(DEV), w, w_form=form, layout=lay, h_from_rounded=True,
+                                want_preact=want_preact)
+    finally:
+        _lib.set_gemm_path(0)
+    acc = x.float() @ w_rows.float().t()
+    ref_pre = O._round(acc, True)
+    ref_h = O.forward_logic(ref_pre, layout, True)
+    assert O.rel_max(full_pre.cpu(), ref_pre) <= BF16_TOL
+    assert O.rel_max(full_h.cpu(), ref_h) <= BF16_TOL
+    assert torch.equal(h, full_h)
+    assert (pre is None) == (not want_preact)
