@@ -30,6 +30,15 @@
 //                and, if out1 is set, h = left * silu(gate) of the preact it
 //                read into out1 [M, H] (swiglu_recompute.py:71), the operand
 //                of a plain dW2 GEMM
+//   kEpiScatterRows  tensor-parallel: f32 rows pushed into their owner
+//                rank's receive buffer (see epilogue_tile)
+//   kEpiSwigluTma    kEpiSwiglu storing through shared memory and TMA
+//                (2-SM kernel only)
+// In the 2-SM kernel (tc_gemm2.cuh) the store, SwiGLU-TMA and dSwiGLU
+// epilogues move their tiles as {32 x 32} boxes through swizzled shared
+// memory and TMA (epilogue_store_tma, epilogue_swiglu_tma,
+// epilogue_dswiglu_tma); the per-lane forms below serve the single-SM kernel
+// and the small-M forward.
 // The dW2 GEMM with the h prologue is a separate kernel (tc_dw2.cuh).
 #pragma once
 

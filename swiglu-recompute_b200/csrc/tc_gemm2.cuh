@@ -16,8 +16,13 @@
 //   rank 0's MMA thread waits `full[s]`, issues the pair MMAs and commits to
 //     `empty[s]` of both CTAs, and per tile to `tmem_full[acc]` of both CTAs;
 //   both CTAs' epilogue warps drain their TMEM rows and arrive on rank 0's
-//     `tmem_empty[acc]` (8 arrivals: 4 warps x 2 CTAs).
-// Epilogues are the same as the single-SM kernel's (epilogue_tile).
+//     `tmem_empty[acc]` (8 arrivals: 4 warps x 2 CTAs); with NSUB = 2 the
+//     single accumulator's two 256-column halves are freed one by one
+//     (`tmem_empty[0]`, `[1]`) and the MMA thread starts the next tile on
+//     half 0 while half 1 drains.
+// Epilogues: each 256-column half is written as a tile of its own; plain
+// stores, SwiGLU (kEpiSwigluTma) and dSwiGLU go through swizzled shared-memory
+// boxes and TMA (tc_gemm.cuh), the rest through epilogue_tile.
 //
 // No TMA multicast is used: each CTA loads its own halves.
 #pragma once
