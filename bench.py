@@ -41,6 +41,14 @@ import torch  # noqa: E402
 CFG = dict(M=11136, D=3584, H=14336, Dout=3584)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "SwiGLU-MLP fwd+bwd TFLOP/s (bf16, M=11136 D=3584 H=14336 Dout=3584)"
+# The tensor-parallel configuration (Llama-3-70B MLP shape, 1/2/4/8 GPUs):
+# `--workload cfg5`, measured beside the bench line, not instead of it.
+CFG5 = dict(M=65536, D=8192, H=28672, Dout=8192)
+WORKLOADS = {
+    "cfg2": (CFG, METRIC, "cfg2: one SwiGLU MLP block fwd+bwd"),
+    "cfg5": (CFG5, "SwiGLU-MLP fwd+bwd TFLOP/s (bf16, M=65536 D=8192 H=28672 Dout=8192)",
+             "cfg5: one SwiGLU MLP block fwd+bwd, Llama-3-70B MLP shape"),
+}
 
 
 def flops_fwd_bwd(M, D, H, Dout):
@@ -165,10 +173,13 @@ def run_reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------- GPU arm
-def _inputs(dev, dtype=torch.bfloat16):
-    from swiglu_b200.synthetic import make_inputs
-    x, w1, w2, gy = make_inputs(CFG["M"], CFG["D"], CFG["H"], CFG["Dout"], seed=0, dtype=dtype)
-    return x, w1, w2, gy
+def _inputs(dev, dtype=torch.bfloat16, cfg=CFG):
+    """Config 2: drawn on the host (the bits every backend and test sees).
+    Config 5 (7 GiB of f32 draws): drawn on `dev`, same distributions."""
+    from swiglu_b200.synthetic import make_inputs, make_inputs_on_device
+    if cfg is CFG5:
+        return make_inputs_on_device(cfg["M"], cfg["D"], cfg["H"], cfg["Dout"], dev, seed=0, dtype=dtype)
+    return make_inputs(cfg["M"], cfg["D"], cfg["H"], cfg["Dout"], seed=0, dtype=dtype)
 
 
 def kernel_breakdown(x, w1, w2, gy, iters):
@@ -343,6 +354,85 @@ def run_stack_sweep(args):
                                                   "ms_per_step": REFERENCE_STACK_MS[n]}}), flush=True)
 
 
+def run_power_sweep(args):
+    """Sustained load (about 3 s per arm, long enough for the 1 kW power cap to
+    set the clock) on one GPU at `--workload`'s shape: the six-kernel step with
+    the tile widths the library picks, with every GEMM on 256 x 256 and on
+    256 x 512 tiles, and the eager PyTorch MLP (cuBLAS GEMMs + pointwise) for
+    comparison. Per arm: ms per step and per kernel over the last two thirds
+    of the steps (CUDA events) and the sampled clocks. One JSON line per arm;
+    not the bench line."""
+    from swiglu_b200 import _lib, ops
+    from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg, _, workload = WORKLOADS[args.workload]
+    M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
+    x, w1, w2, gy = (t.to(dev) for t in _inputs(dev, cfg=cfg))
+    fl = flops_fwd_bwd(M, D, H, Dout)
+    names = ["gemm1_swiglu", "gemm2_y", "gradh_dswiglu_emit_h", "dw2_gemm", "dw1", "dx"]
+
+    def ours(ev):
+        ev[0].record()
+        preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+        ev[1].record()
+        y = ops.matmul(h, w2, a_t=False, b_t=True)
+        ev[2].record()
+        del y
+        ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD, h_out=h)
+        ev[3].record()
+        dw2 = ops.matmul(gy, h, a_t=True, b_t=False)
+        ev[4].record()
+        del h
+        dw1 = ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512)
+        ev[5].record()
+        dx = ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512)
+        ev[6].record()
+        return dw2, dw1, dx
+
+    W1 = w1.detach().clone().requires_grad_(True)
+    W2 = w2.detach().clone().requires_grad_(True)
+
+    def torch_mlp(ev):
+        ev[0].record()
+        xi = x.detach().requires_grad_(True)
+        left, gate = (xi @ W1.t()).chunk(2, dim=-1)
+        y = (left * torch.nn.functional.silu(gate)) @ W2.t()
+        out = torch.autograd.grad(y, [xi, W1, W2], gy)
+        ev[6].record()
+        return out
+
+    est_ms = fl / 1.2e12   # one step at ~1.2 PFLOP/s
+    arms = [("library", ours, 0), ("all_256x256", ours, 2), ("all_256x512", ours, 3),
+            ("torch_eager_cublas", torch_mlp, 0)]
+    for name, fn, path in arms:
+        _lib.set_gemm_path(path)
+        try:
+            dummy = [torch.cuda.Event() for _ in range(7)]
+            for _ in range(3):
+                fn(dummy)
+            torch.cuda.synchronize()
+            n = max(9, int(3000.0 / est_ms))
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(n)]
+            with ClockSampler(0) as clk:
+                time.sleep(0.3)
+                for i in range(n):
+                    fn(evs[i])
+                torch.cuda.synchronize()
+        finally:
+            _lib.set_gemm_path(0)
+        tail = evs[n // 3:]
+        ms = sum(e[0].elapsed_time(e[6]) for e in tail) / len(tail)
+        line = {"sweep": "power", "workload": workload, **cfg, "arm": name, "steps": n,
+                "ms_per_step": round(ms, 4), "tflops": round(fl / ms / 1e9, 1), "clocks": clk.summary()}
+        if fn is ours:
+            line["kernels_ms"] = {k: round(sum(e[i].elapsed_time(e[i + 1]) for e in tail) / len(tail), 4)
+                                  for i, k in enumerate(names)}
+        print(json.dumps(line), flush=True)
+    assert ops.device_status(0) == 0
+
+
 def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom", compile_model=False):
     """Peak allocated-memory delta (MiB) and ms per fwd+bwd of `n_blocks`
     stacked config-2 blocks, measured as the reference's stacked-depth
@@ -465,8 +555,9 @@ def run_ours_single(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    M, D, H, Dout = CFG["M"], CFG["D"], CFG["H"], CFG["Dout"]
-    x, w1, w2, gy = _inputs(dev)
+    cfg, metric, workload = WORKLOADS[args.workload]
+    M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
+    x, w1, w2, gy = _inputs(dev, cfg=cfg)
     model = SR.SwiGLUMLPCustom(D, H, Dout, dtype=torch.bfloat16).to(dev)
     with torch.no_grad():
         model.w1.copy_(w1)
@@ -518,7 +609,7 @@ def run_ours_single(args):
     # its x and grad_y in from pinned host memory and its grad_x out, on a copy
     # stream that runs one step ahead (inputs of step i+1 and the output of
     # step i move while step i+1 / i computes), as a data loader would.
-    e2e_ms, h2d, d2h = e2e_pipelined(model, params, x, gy, dev, args)
+    e2e_ms, h2d, d2h = e2e_pipelined(model, params, x.cpu(), gy.cpu(), dev, args)
 
     # Per-kernel device times on the launching stream; dominant kernel roofline.
     w1d, w2d = model.w1.detach(), model.w2.detach()
@@ -531,19 +622,20 @@ def run_ours_single(args):
     assert ops.device_status(0) == 0, "kernel pipeline timeout"
 
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": "cfg2: one SwiGLU MLP block fwd+bwd, recompute Function", **CFG,
-                   "parallelism": "tp1", "l2": "working set > L2 (preact alone 609 MiB)"},
+        "data": "synthetic" if cfg is CFG else "synthetic, drawn on the device",
+        "config": {"workload": workload + ", recompute Function", **cfg, "parallelism": "tp1",
+                   "l2": f"working set > L2 (preact alone {M * 2 * H * 2 / 2**20:.0f} MiB)"},
         "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": 6 * args.steps,
         "frac_of_peak": {"sustained": round(value / peak, 4),
                          "burst": round(value / float(peaks["bf16_tflops"]), 4), "source": peak_src},
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(ach / peak, 4), "traffic": profile_traffic(dom),
+                     "unit": "TFLOP/s", "frac": round(ach / peak, 4),
+                     "traffic": profile_traffic(dom) if cfg is CFG else None,
                      "peak_kind": f"bf16_tflops_sustained ({peak_src})"},
         "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
         "variants": {"dw2_prologue": {"ms_per_step": round(ms_prologue, 4),
@@ -552,7 +644,7 @@ def run_ours_single(args):
                                               "no [M, H] buffer in backward"}},
         "clocks": clk.summary(),
     }
-    if not args.no_stack:
+    if not args.no_stack and cfg is CFG:
         peak, sms = stacked_depth(8, dev)
         line["stacked"] = {"n_blocks": 8, "peak_mib": round(peak, 1), "ms_per_step": round(sms, 3),
                            "reference_recompute_peak_mib": REFERENCE_STACK_PEAK_MIB[8],
@@ -567,7 +659,7 @@ def run_ours_single(args):
         peak_fc, ms_fc = stacked_depth(8, dev, module="SwiGLUMLPFullCheckpoint")
         line["stacked_full_checkpoint"] = {"n_blocks": 8, "peak_mib": round(peak_fc, 1),
                                            "ms_per_step": round(ms_fc, 3)}
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and cfg is CFG:
         tf, cores, sample = cpu_reference_sample(seconds=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                 "sample": sample}
@@ -590,6 +682,11 @@ def main():
                     help="forward-only W1 projection + SwiGLU vs cuBLAS, config 3 M sweep (not the bench line)")
     ap.add_argument("--stack-sweep", action="store_true",
                     help="stacked-depth memory and time at N = 1..16 blocks, config 4 (not the bench line)")
+    ap.add_argument("--power-sweep", action="store_true",
+                    help="sustained-load tile-width and PyTorch comparison at --workload (not the bench line)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
+                    help="cfg2: the bench line's single block; cfg5: the tensor-parallel configuration "
+                         "(M=65536 D=8192 H=28672 Dout=8192) at 1/2/4/8 GPUs")
     ap.add_argument("--gemm-path", type=int, choices=[0, 1, 2, 3], default=0,
                     help="tcgen05 kernel family: 0 by size, 1 single-SM, 2 CTA pair 256x256, 3 CTA pair 256x512")
     args = ap.parse_args()
@@ -610,6 +707,9 @@ def main():
     if args.stack_sweep:
         run_stack_sweep(args)
         return
+    if args.power_sweep:
+        run_power_sweep(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
@@ -618,8 +718,11 @@ def main():
         print(json.dumps(line), flush=True)
         return
     from swiglu_b200 import tp
-    line = tp.bench_tp(args, CFG, flops_fwd_bwd, METRIC, ClockSampler, load_peaks, cpu_reference_sample,
-                       e2e_pipelined)
+    cfg, metric, workload = WORKLOADS[args.workload]
+    line = tp.bench_tp(args, cfg, flops_fwd_bwd, metric, ClockSampler, load_peaks, cpu_reference_sample,
+                       e2e_pipelined, workload=workload,
+                       inputs_fn=lambda dev: _inputs(dev, cfg=cfg),
+                       data="synthetic" if cfg is CFG else "synthetic, drawn on the device")
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -119,11 +119,13 @@ int swiglu_b200_matmul(const void* a, const void* b, void* c, int64_t M, int64_t
                        int b_layout, int dtype, int out_dtype, int group_size_m, void* stream);
 
 /* swiglu_b200_matmul with a preferred output-tile width for the 2-SM kernel:
- * tile_n = 0 or 256 (the default 256 x 256 tiles, accumulator double-buffered
- * in TMEM) or 512 (256 x 512 tiles: a quarter fewer operand bytes per FLOP,
- * epilogue between main loops), used for the backward's long-K GEMMs
- * dW1 = grad_preact^T . x and dx = grad_preact . W1 (swiglu_recompute.py:76-77).
- * A path forced with swiglu_b200_set_gemm_path takes precedence. */
+ * tile_n = 256 (256 x 256 tiles, accumulator double-buffered in TMEM), 512
+ * (256 x 512 tiles: a quarter fewer operand bytes per FLOP, epilogue between
+ * main loops; used for the backward's long-K GEMMs dW1 = grad_preact^T . x
+ * and dx = grad_preact . W1, swiglu_recompute.py:76-77) or 0 (by size: 512
+ * once the 256 x 512 tiles make 8 waves of CTA pairs, else 256; this is what
+ * swiglu_b200_matmul does). A path forced with swiglu_b200_set_gemm_path takes
+ * precedence. */
 int swiglu_b200_matmul_tiled(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int a_layout,
                              int b_layout, int dtype, int out_dtype, int group_size_m, int tile_n, void* stream);
 

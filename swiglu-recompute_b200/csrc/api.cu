@@ -411,9 +411,9 @@ int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
 // the 2-SM (256-row tiles) kernel. p.tiles_n must be set; tiles_m is set here.
-// `tile_n` is the caller's preference for the pair tile's width (0 = the
-// 256-column default, 512 = 256 x 512 tiles); it applies where the size rule
-// picks the 2-SM kernel and no path is forced with swiglu_b200_set_gemm_path.
+// `tile_n` is the caller's preference for the pair tile's width (256 or 512;
+// 0 = by size, below); it applies where the size rule picks the 2-SM kernel
+// and no path is forced with swiglu_b200_set_gemm_path.
 template <bool A_MN, bool B_MN, int EPI, bool F32>
 int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) {
   const int tiles2 = ((p.M + 255) / 256) * p.tiles_n;
@@ -421,7 +421,17 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) 
   // The 2-SM dSwiGLU epilogue stores 32-column TMA boxes: whole chunks only.
   if (EPI == kEpiDswiglu && !(p.flags & kFlagTmaEpilogue)) mode = 1;
   // By size: pairs pay off once there is at least one full wave of them.
-  if (mode == 0) mode = tiles2 >= d.sms / 2 ? (tile_n == 512 ? 3 : 2) : 1;
+  // Plain-store GEMMs without a width preference take 256 x 512 tiles once
+  // those make 8 waves of pairs: at M=65536 D=8192 H=28672 (y: 55 waves,
+  // dW2: 24) they measured 17 % faster than 256 x 256 tiles at equal clocks,
+  // while at 4-5 waves (y and dW2 at M=11136 D=3584 H=14336) the 256-column
+  // tiles are faster.
+  if (mode == 0) {
+    const long long tiles512 = static_cast<long long>((p.M + 255) / 256) * ((p.tiles_n + 1) / 2);
+    const bool wide =
+        tile_n == 512 || (tile_n == 0 && EPI == kEpiStore && tiles512 >= 8LL * (d.sms / 2));
+    mode = tiles2 >= d.sms / 2 ? (wide ? 3 : 2) : 1;
+  }
   if (mode == 2 || mode == 3) {
     // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
     // fused_forward.py:58); a pair tile covers two of them.

@@ -145,7 +145,8 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool, b_t: bool,
            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
            group_size_m: int = DEFAULT_GROUP_M, tile_n: int = 0) -> torch.Tensor:
     """C = op(a) . op(b); op(a) = a.T if a_t, op(b) = b.T if b_t. tile_n = 512
-    asks the 2-SM kernel for 256 x 512 output tiles (long-K GEMMs)."""
+    asks the 2-SM kernel for 256 x 512 output tiles (long-K GEMMs), 256 for
+    256 x 256; 0 chooses by size (512 from 8 waves of 256 x 512 tiles)."""
     dev = _check_cuda(a, b, out)
     dt = _same_dtype(a, b)
     M, K = (a.shape[1], a.shape[0]) if a_t else tuple(a.shape)

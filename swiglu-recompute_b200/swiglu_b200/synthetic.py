@@ -17,3 +17,19 @@ def make_inputs(M: int, D: int, H: int, Dout: int, seed: int = 0, dtype=torch.fl
     w2 = torch.randn(Dout, H, generator=g) * H ** -0.5
     gy = torch.randn(M, Dout, generator=g)
     return tuple(t.to(dtype) for t in (x, w1, w2, gy))
+
+
+def make_inputs_on_device(M: int, D: int, H: int, Dout: int, device, seed: int = 0,
+                          dtype=torch.bfloat16):
+    """The same distributions drawn by a generator on `device` (no host copy of
+    the f32 draws, for shapes whose inputs are gigabytes). The bits differ from
+    `make_inputs`; every rank that passes the same seed gets the same tensors."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for shape, scale in (((M, D), 1.0), ((2 * H, D), D ** -0.5), ((Dout, H), H ** -0.5), ((M, Dout), 1.0)):
+        t = torch.randn(*shape, generator=g, device=device)
+        if scale != 1.0:
+            t.mul_(scale)
+        out.append(t.to(dtype))
+        del t
+    return tuple(out)

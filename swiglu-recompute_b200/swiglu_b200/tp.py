@@ -195,8 +195,8 @@ class NativeCompute:
         return ops.swiglu_fwd(x, w1_local, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
 
     @staticmethod
-    def matmul(a, b, *, a_t, b_t, out_dtype=None):
-        return ops.matmul(a, b, a_t=a_t, b_t=b_t, out_dtype=out_dtype)
+    def matmul(a, b, *, a_t, b_t, out_dtype=None, tile_n=0):
+        return ops.matmul(a, b, a_t=a_t, b_t=b_t, out_dtype=out_dtype, tile_n=tile_n)
 
     @staticmethod
     def dw2(gy, preact):
@@ -250,12 +250,14 @@ class _TPSwiGLUFunction(torch.autograd.Function):
             pending = ctx.fused_rs.matmul_start("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
         else:
             acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
-            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt),
-                                            ctx.group)
+            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt,
+                                                           tile_n=512), ctx.group)
         if h is not None:
             dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
             del h
-        dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
+        # dW1 and dx are the long-K GEMMs: 256 x 512 pair tiles, as in the
+        # single-GPU backward (swiglu_recompute._recompute_backward).
+        dw1 = compute.matmul(gp, x, a_t=True, b_t=False, tile_n=512)
         if fused:
             dx_local = ctx.fused_rs.finish(pending)
         else:
@@ -307,9 +309,11 @@ class SwiGLUMLPTensorParallel(nn.Module):
 
 
 # -------------------------------------------------------------- bench
-def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e_fn):
-    """Strong-scaling TP run of the config-2 block on WORLD_SIZE GPUs (one
-    process per GPU). Returns the JSON dict on rank 0, None elsewhere."""
+def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e_fn, *,
+             workload="cfg2: one SwiGLU MLP block fwd+bwd", inputs_fn=None, data="synthetic"):
+    """Strong-scaling TP run of one block of shape `cfg` on WORLD_SIZE GPUs (one
+    process per GPU). `inputs_fn(device)` draws (x, W1, W2, grad_y) (default:
+    on the host). Returns the JSON dict on rank 0, None elsewhere."""
     from swiglu_b200.synthetic import make_inputs
 
     rank = int(os.environ.get("RANK", "0"))
@@ -322,7 +326,10 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e
     try:
         M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
         assert M % world == 0 and H % world == 0
-        x, w1, w2, gy = make_inputs(M, D, H, Dout, seed=0, dtype=torch.bfloat16)
+        if inputs_fn is None:
+            x, w1, w2, gy = make_inputs(M, D, H, Dout, seed=0, dtype=torch.bfloat16)
+        else:
+            x, w1, w2, gy = inputs_fn(dev)
         ms_rows = M // world
         fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
         model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
@@ -379,8 +386,8 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e
             "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": "cfg2: one SwiGLU MLP block fwd+bwd, tensor parallel", **cfg,
+            "data": data,
+            "config": {"workload": workload + ", tensor parallel", **cfg,
                        "parallelism": f"tp{world}",
                        "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
                                   if fused else "f32 partials, NCCL reduce-scatter"),

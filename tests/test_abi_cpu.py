@@ -86,3 +86,19 @@ def test_synthetic_inputs_match_the_oracle_draw():
     for shape, seed, dtype in [((64, 48, 40, 24), 0, torch.float32), ((33, 16, 8, 8), 7, torch.bfloat16)]:
         for a, b in zip(make_inputs(*shape, seed=seed, dtype=dtype), O.make_inputs(*shape, seed=seed, dtype=dtype)):
             assert torch.equal(a, b)
+
+
+def test_device_drawn_inputs_have_the_configured_distributions():
+    """The large-shape draw (on the device; here on the CPU generator): same
+    shapes, dtype and scales as make_inputs, reproducible for a seed."""
+    from swiglu_b200.synthetic import make_inputs_on_device
+
+    M, D, H, Dout = 512, 256, 384, 128
+    a = make_inputs_on_device(M, D, H, Dout, "cpu", seed=3)
+    b = make_inputs_on_device(M, D, H, Dout, "cpu", seed=3)
+    assert [t.shape for t in a] == [(M, D), (2 * H, D), (Dout, H), (M, Dout)]
+    assert all(t.dtype == torch.bfloat16 for t in a)
+    assert all(torch.equal(u, v) for u, v in zip(a, b))
+    for t, std in zip(a, (1.0, D ** -0.5, H ** -0.5, 1.0)):
+        assert abs(t.float().std().item() / std - 1.0) < 0.05
+        assert abs(t.float().mean().item()) < 0.05 * std

@@ -22,7 +22,7 @@ class OracleCompute:
         return preact, O.forward_logic(preact)
 
     @staticmethod
-    def matmul(a, b, *, a_t, b_t, out_dtype=None):
+    def matmul(a, b, *, a_t, b_t, out_dtype=None, tile_n=0):
         out = (a.t() if a_t else a) @ (b.t() if b_t else b)
         return out.to(out_dtype) if out_dtype is not None else out
 
