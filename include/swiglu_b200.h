@@ -76,6 +76,14 @@ int swiglu_b200_device_status(uint32_t* bits, int clear);
  * their tiling at compile time, fused_forward.py:55-65). */
 int swiglu_b200_set_gemm_path(int mode);
 
+/* The kernel family swiglu_b200_matmul_tiled would run a bf16 GEMM with an
+ * [M, N] output on, for a device with `num_sms` SMs: *family = 1 (single-SM),
+ * 2 (CTA pair, 256 x 256 tiles) or 3 (CTA pair, 256 x 512 tiles), honouring a
+ * path forced with swiglu_b200_set_gemm_path. Host-only (no device call). No
+ * reference counterpart (Triton autotuning picks tiles inside the launch,
+ * fused_forward.py:55-65). */
+int swiglu_b200_gemm_plan(int64_t M, int64_t N, int tile_n, int num_sms, int* family);
+
 /* Recommended size of a stream-K workspace (48 MiB). */
 #define SWIGLU_B200_STREAM_WORKSPACE_BYTES ((size_t)48 << 20)
 

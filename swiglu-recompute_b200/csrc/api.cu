@@ -409,6 +409,24 @@ int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
   return launch_pair<kern>(p, tiles + p.sk_tail * (p.sk_split - 1), Cfg::NUM_THREADS, Cfg::SMEM_BYTES, d, st, what);
 }
 
+// Kernel family for one tcgen05 GEMM: 1 = single-SM (128-row tiles), 2 = CTA
+// pair with 256 x 256 tiles, 3 = CTA pair with 256 x 512 tiles. `forced` is
+// the process-wide path (0 = by size), `tiles_n` the output's 256-column
+// tiles. By size, pairs pay off once there is at least one full wave of them.
+// Plain-store GEMMs without a width preference take 256 x 512 tiles once
+// those make 8 waves of pairs: at M=65536 D=8192 H=28672 (y: 55 waves,
+// dW2: 24) they measured 17 % faster than 256 x 256 tiles at equal clocks,
+// while at 4-5 waves (y and dW2 at M=11136 D=3584 H=14336) the 256-column
+// tiles are faster.
+int pick_gemm_mode(int64_t M, int64_t tiles_n, bool plain_store, int tile_n, int sms, int forced) {
+  if (forced != 0) return forced;
+  const int64_t tiles_m2 = (M + 255) / 256;
+  const int64_t pairs = sms / 2;
+  if (tiles_m2 * tiles_n < pairs) return 1;
+  const bool wide = tile_n == 512 || (tile_n == 0 && plain_store && tiles_m2 * ((tiles_n + 1) / 2) >= 8 * pairs);
+  return wide ? 3 : 2;
+}
+
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
 // the 2-SM (256-row tiles) kernel. p.tiles_n must be set; tiles_m is set here.
 // `tile_n` is the caller's preference for the pair tile's width (256 or 512;
@@ -416,22 +434,10 @@ int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
 // and no path is forced with swiglu_b200_set_gemm_path.
 template <bool A_MN, bool B_MN, int EPI, bool F32>
 int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) {
-  const int tiles2 = ((p.M + 255) / 256) * p.tiles_n;
   int mode = g_gemm_path.load(std::memory_order_relaxed);
   // The 2-SM dSwiGLU epilogue stores 32-column TMA boxes: whole chunks only.
   if (EPI == kEpiDswiglu && !(p.flags & kFlagTmaEpilogue)) mode = 1;
-  // By size: pairs pay off once there is at least one full wave of them.
-  // Plain-store GEMMs without a width preference take 256 x 512 tiles once
-  // those make 8 waves of pairs: at M=65536 D=8192 H=28672 (y: 55 waves,
-  // dW2: 24) they measured 17 % faster than 256 x 256 tiles at equal clocks,
-  // while at 4-5 waves (y and dW2 at M=11136 D=3584 H=14336) the 256-column
-  // tiles are faster.
-  if (mode == 0) {
-    const long long tiles512 = static_cast<long long>((p.M + 255) / 256) * ((p.tiles_n + 1) / 2);
-    const bool wide =
-        tile_n == 512 || (tile_n == 0 && EPI == kEpiStore && tiles512 >= 8LL * (d.sms / 2));
-    mode = tiles2 >= d.sms / 2 ? (wide ? 3 : 2) : 1;
-  }
+  mode = pick_gemm_mode(p.M, p.tiles_n, EPI == kEpiStore, tile_n, d.sms, mode);
   if (mode == 2 || mode == 3) {
     // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
     // fused_forward.py:58); a pair tile covers two of them.
@@ -1022,6 +1028,16 @@ int swiglu_b200_matmul_reduce_rows_noalloc(const void* a, const void* b, void* o
 
 int swiglu_b200_set_stream_workspace(void* workspace, size_t bytes, void* stream) {
   return set_workspace(workspace, bytes, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_gemm_plan(int64_t M, int64_t N, int tile_n, int num_sms, int* family) {
+  if (!family) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (tile_n != 0 && tile_n != 256 && tile_n != 512)
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "tile_n must be 0, 256 or 512");
+  if (int rc = check_dims("gemm_plan", M, N, 1)) return rc;
+  if (num_sms < 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "num_sms must be >= 2");
+  *family = pick_gemm_mode(M, (N + 255) / 256, true, tile_n, num_sms, g_gemm_path.load(std::memory_order_relaxed));
+  return SWIGLU_OK;
 }
 
 int swiglu_b200_set_gemm_path(int mode) {

@@ -30,6 +30,7 @@ _SIGNATURES = {
     "swiglu_b200_last_error_message": [],
     "swiglu_b200_device_status": [ctypes.POINTER(ctypes.c_uint32), _i],
     "swiglu_b200_set_gemm_path": [_i],
+    "swiglu_b200_gemm_plan": [_i64, _i64, _i, _i, ctypes.POINTER(_i)],
     "swiglu_b200_set_stream_workspace": [_p, ctypes.c_size_t, _p],
     "swiglu_b200_fused_matmul_swiglu_save_preact":
         [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
@@ -111,6 +112,14 @@ def set_gemm_path(mode: int) -> None:
     """0 = by size, 1 = single-SM tcgen05 kernel, 2 = 2-SM (CTA pair) kernel with 256 x 256
     tiles, 3 = 2-SM kernel with 256 x 512 tiles."""
     call("swiglu_b200_set_gemm_path", int(mode))
+
+
+def gemm_plan(M: int, N: int, tile_n: int = 0, num_sms: int = 148) -> int:
+    """Kernel family of a bf16 GEMM with an [M, N] output: 1 = single-SM,
+    2 = CTA pair 256 x 256 tiles, 3 = CTA pair 256 x 512 tiles (host-only)."""
+    fam = ctypes.c_int(0)
+    call("swiglu_b200_gemm_plan", int(M), int(N), int(tile_n), int(num_sms), ctypes.byref(fam))
+    return int(fam.value)
 
 
 def device_status(clear: bool = True) -> int:

@@ -102,3 +102,32 @@ def test_device_drawn_inputs_have_the_configured_distributions():
     for t, std in zip(a, (1.0, D ** -0.5, H ** -0.5, 1.0)):
         assert abs(t.float().std().item() / std - 1.0) < 0.05
         assert abs(t.float().mean().item()) < 0.05 * std
+
+
+@pytest.mark.parametrize("M,N,tile_n,family", [
+    (11136, 3584, 0, 2),     # config 2 y = h . W2^T: 4 waves of 256 x 512 tiles -> 256 x 256
+    (3584, 14336, 0, 2),     # config 2 dW2: 5 waves -> 256 x 256
+    (28672, 3584, 0, 3),     # config 2 dW1 shape: 10.6 waves -> 256 x 512 even without the hint
+    (11136, 3584, 512, 3),   # config 2 dx with the backward's hint
+    (65536, 8192, 0, 3),     # config 5 y: 55 waves
+    (8192, 28672, 0, 3),     # config 5 dW2: 24 waves
+    (65536, 8192, 256, 2),   # an explicit 256 keeps the narrow tiles
+    (65536, 2048, 0, 3),     # the GPU size-rule tests' shapes
+    (4096, 20480, 0, 3),
+    (2560, 4096, 0, 2),      # the stream-K test shape
+    (256, 512, 0, 1),        # less than a wave of pairs -> single-SM kernel
+])
+def test_gemm_plan_size_rule(M, N, tile_n, family):
+    """The kernel-family choice of the plain GEMM, host-only, on a 148-SM B200."""
+    assert _lib.gemm_plan(M, N, tile_n, 148) == family
+
+
+def test_gemm_plan_honours_forced_path_and_rejects_bad_widths():
+    try:
+        for mode in (1, 2, 3):
+            _lib.set_gemm_path(mode)
+            assert _lib.gemm_plan(65536, 8192) == mode
+    finally:
+        _lib.set_gemm_path(0)
+    with pytest.raises(_lib.SwigluError, match="tile_n"):
+        _lib.gemm_plan(1024, 1024, 384)
