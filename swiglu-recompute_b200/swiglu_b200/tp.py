@@ -376,6 +376,11 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e
         status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
         dist.all_reduce(status, op=dist.ReduceOp.MAX)
         dist.barrier()
+        # This library's launches per rank and step: GEMM1, y, grad_h, dW2, dW1,
+        # dx, plus a signal and an owner-reduce kernel for each GEMM that
+        # carries its reduce-scatter (y with K = H/t, dx with K = 2H/t).
+        frs = model.fused_rs if isinstance(model.fused_rs, FusedReduceScatter) else None
+        launches = 6 + (2 * sum(frs.wants(k) for k in (H // world, 2 * H // world)) if frs else 0)
         if rank != 0:
             return None
         fl = flops_fn(M, D, H, Dout)
@@ -395,7 +400,7 @@ def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
-            "gpu_launches": 6 * args.steps * world,
+            "gpu_launches": launches * args.steps * world,
             "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
             "device_status": int(status.item()),
             "clocks": clk.summary(),
