@@ -250,14 +250,15 @@ class _TPSwiGLUFunction(torch.autograd.Function):
             pending = ctx.fused_rs.matmul_start("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
         else:
             acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
-            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt,
-                                                           tile_n=512), ctx.group)
+            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt),
+                                            ctx.group)
         if h is not None:
             dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
             del h
-        # dW1 and dx are the long-K GEMMs: 256 x 512 pair tiles, as in the
-        # single-GPU backward (swiglu_recompute._recompute_backward).
-        dw1 = compute.matmul(gp, x, a_t=True, b_t=False, tile_n=512)
+        # Tile widths of the local GEMMs by size (256 x 512 from 8 waves of
+        # them): the per-rank dW1 of a sharded block is 1/t of the
+        # single-GPU one, often below the size where the wide tiles win.
+        dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
         if fused:
             dx_local = ctx.fused_rs.finish(pending)
         else:
