@@ -133,12 +133,12 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU arm
-def cpu_reference_sample(seconds=12.0, rows=256):
+def cpu_reference_sample(seconds=12.0, rows=256, cfg=CFG):
     """The reference's fp32 path (oracle restatement) on this host's cores, on a
-    `rows`-row slice of the config-2 shapes. Returns (TFLOP/s, cores, sample)."""
+    `rows`-row slice of `cfg`'s shapes. Returns (TFLOP/s, cores, sample)."""
     from oracle import swiglu_oracle as O
 
-    D, H, Dout = CFG["D"], CFG["H"], CFG["Dout"]
+    D, H, Dout = cfg["D"], cfg["H"], cfg["Dout"]
     torch.set_num_threads(os.cpu_count() or 1)
     x, w1, w2, gy = O.make_inputs(rows, D, H, Dout, seed=0, dtype=torch.float32)
     O.mlp_forward_backward(x[:16], w1, w2, gy[:16])            # warm-up
@@ -151,19 +151,21 @@ def cpu_reference_sample(seconds=12.0, rows=256):
         times.append(time.perf_counter() - t0)
     best = min(times)
     return fl / best / 1e12, torch.get_num_threads(), (
-        f"fp32 fwd+bwd of {rows} of {CFG['M']} rows at D={D} H={H} Dout={Dout}, "
+        f"fp32 fwd+bwd of {rows} of {cfg['M']} rows at D={D} H={H} Dout={Dout}, "
         f"best of {len(times)} (wall clock)")
 
 
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    tf, cores, sample = cpu_reference_sample(seconds=max(6.0, 2.0 * (args.steps + args.warmup)))
+    cfg, metric, workload = WORKLOADS[args.workload]
+    tf, cores, sample = cpu_reference_sample(seconds=max(6.0, 2.0 * (args.steps + args.warmup)), cfg=cfg)
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(tf, 4), "unit": "TFLOP/s",
+        "impl": "reference", "metric": metric, "value": round(tf, 4), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 single SwiGLU block fwd+bwd (row sample)", **CFG},
+        "config": {"workload": workload + ", reference fp32 path on the host cores (row sample)", **cfg,
+                   "parallelism": "one host process"},
         "cpu_baseline": {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(tf, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
