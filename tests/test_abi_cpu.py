@@ -1,6 +1,7 @@
 """The C-ABI library: loads without a GPU, exports every header symbol, and
 rejects bad arguments before touching the device. CPU only (no compute calls)."""
 import ctypes
+import os
 
 import pytest
 import torch
@@ -131,3 +132,49 @@ def test_gemm_plan_honours_forced_path_and_rejects_bad_widths():
         _lib.set_gemm_path(0)
     with pytest.raises(_lib.SwigluError, match="tile_n"):
         _lib.gemm_plan(1024, 1024, 384)
+
+
+C_CALLER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "swiglu_b200.h"
+
+int main(void) {
+  int fam = 0;
+  if (swiglu_b200_abi_version() <= 0) return 10;
+  if (swiglu_b200_gemm_plan(65536, 8192, 0, 148, &fam) != SWIGLU_OK || fam != 3) return 11;
+  if (swiglu_b200_gemm_plan(11136, 3584, 0, 148, &fam) != SWIGLU_OK || fam != 2) return 12;
+  if (swiglu_b200_gemm_plan(1024, 1024, 384, 148, &fam) != SWIGLU_ERR_INVALID_ARGUMENT) return 13;
+  if (!strstr(swiglu_b200_last_error_message(), "tile_n")) return 14;
+  if (strcmp(swiglu_b200_status_string(SWIGLU_OK), "SWIGLU_OK") != 0) return 15;
+  /* a null device pointer is rejected before any device work */
+  if (swiglu_b200_matmul(NULL, NULL, NULL, 256, 256, 64, 0, 0, SWIGLU_BF16, SWIGLU_BF16, 8, NULL)
+      != SWIGLU_ERR_INVALID_ARGUMENT) return 16;
+  printf("ok %d\n", swiglu_b200_abi_version());
+  return 0;
+}
+"""
+
+
+def test_header_compiles_as_c99_and_a_c_caller_links(tmp_path):
+    """The boundary as a C caller sees it: the header is plain C99, the
+    library links with -lswiglu_b200, and the host-only calls and argument
+    checks behave as documented (no GPU needed)."""
+    import shutil
+    import subprocess
+
+    from swiglu_b200.build import INCLUDE_DIR, LIB_PATH
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "caller.c"
+    src.write_text(C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(LIB_PATH)
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-pedantic", f"-I{INCLUDE_DIR}", str(src),
+                    f"-L{libdir}", "-lswiglu_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                   check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
+    assert out.stdout.startswith("ok ")
