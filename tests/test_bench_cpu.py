@@ -1,0 +1,72 @@
+"""bench.py's host-side logic, with no GPU: the FLOP accounting of both
+workloads, the clock record (throttle reasons and the loaded-sample filter
+over nvidia-smi lines), the warm-up floor, and the reference arm's JSON line
+(the CPU restatement of the reference's fp32 path on a row sample)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+import bench
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_flop_accounting_of_both_workloads():
+    # 6 M (2 H D + H Dout): the reference's accounting (results_fused_forward.md:75)
+    assert bench.flops_fwd_bwd(**bench.CFG) == pytest.approx(10.2991e12, rel=1e-4)
+    assert bench.flops_fwd_bwd(**bench.CFG5) == pytest.approx(277.08e12, rel=1e-4)
+    kf = bench.kernel_flops(**bench.CFG)
+    six = ["gemm1_swiglu", "gemm2_y", "gradh_dswiglu_emit_h", "dw2_gemm", "dw1", "dx"]
+    assert sum(kf[k] for k in six) == pytest.approx(bench.flops_fwd_bwd(**bench.CFG))
+    for name, (cfg, metric, workload) in bench.WORKLOADS.items():
+        assert workload.startswith(name)
+        assert all(f"{k}={v}" in metric for k, v in cfg.items())
+
+
+def _sample(sm, power, reasons=()):
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    flags = ", ".join("Active" if n in reasons else "Not Active" for n in names)
+    return f"0, {sm}, 1965, {power}, 0x0, {flags}"
+
+
+def test_clock_summary_keeps_loaded_samples_and_their_reasons():
+    clk = bench.ClockSampler(0)
+    clk.lines = ([_sample(1965, 120.0)] * 3                                   # idle, before the region
+                 + [_sample(1350, 980.0, ["sw_power_cap"])] * 5
+                 + [_sample(1410, 960.0, ["sw_power_cap"])] * 4
+                 + [_sample(1965, 150.0, ["hw_slowdown"])]                    # idle tail: not counted
+                 + ["garbage line"])
+    s = clk.summary()
+    assert s["loaded_samples"] == 9 and s["samples"] == 13
+    assert s["sm_mhz"] == 1350 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_summary_without_samples_is_none():
+    clk = bench.ClockSampler(0)
+    clk.lines = []
+    assert clk.summary() is None
+
+
+def test_warmup_below_three_is_rejected():
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--warmup", "2"],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode != 0 and "--warmup must be >= 3" in out.stderr
+
+
+def test_reference_arm_prints_one_contract_line():
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "3"], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "TFLOP/s"
+    assert d["higher_is_better"] is True and d["value"] > 0
+    assert {k: d["config"][k] for k in bench.CFG} == bench.CFG
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
