@@ -178,3 +178,43 @@ def test_header_compiles_as_c99_and_a_c_caller_links(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
     assert out.stdout.startswith("ok ")
+
+
+def _header_prototypes():
+    import re
+    with open(_lib.HEADER) as f:
+        text = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    protos = {}
+    for ret, name, params in re.findall(r"\b(int|const char\s*\*)\s*(swiglu_b200_\w+)\s*\(([^)]*)\)\s*;", text):
+        params = " ".join(params.split())
+        protos[name] = ([] if params in ("", "void") else [p.strip() for p in params.split(",")], ret)
+    return protos
+
+
+_SCALARS = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t,
+            "uint32_t": ctypes.c_uint32}
+
+
+def test_binding_signatures_match_the_header_prototypes():
+    """Every ctypes argument list has the header's arity, integer widths and
+    pointer positions, so a Python (or INTEGRATION-style) caller cannot pass
+    an int where the library reads an int64 or a pointer."""
+    protos = _header_prototypes()
+    assert set(protos) == set(_lib._SIGNATURES)
+    for name, (params, ret) in protos.items():
+        argtypes = _lib._SIGNATURES[name]
+        assert len(params) == len(argtypes), name
+        for decl, at in zip(params, argtypes):
+            ctype = decl.rsplit(" ", 1)[0] if not decl.endswith("*") else decl
+            if "*" in decl:
+                assert at is ctypes.c_void_p or issubclass(at, ctypes._Pointer), (name, decl)
+                if issubclass(at, ctypes._Pointer):
+                    # pointee: a pointer (T* const* = an array of pointers) or a scalar
+                    base = ctype.replace("const", "").replace("*", "").split()[0]
+                    pointee_is_ptr = decl.count("*") >= 2
+                    want = ctypes.c_void_p if pointee_is_ptr or base == "void" else _SCALARS[base]
+                    assert at._type_ is want, (name, decl)
+            else:
+                assert at is _SCALARS[ctype.replace("const", "").strip()], (name, decl)
+        want_ret = ctypes.c_char_p if "char" in ret else ctypes.c_int
+        assert _lib._RESTYPES.get(name, ctypes.c_int) is want_ret, name
