@@ -129,3 +129,21 @@ def test_dead_rank_surfaces_as_error():
         if p.is_alive():
             p.kill()
     assert msg != "no error"
+
+
+@pytest.mark.parametrize("world,H,y_fused,dx_fused", [
+    (2, 14336, True, True),      # config 2: the GEMMs' math covers their NVLink push
+    (4, 14336, True, True),
+    (8, 14336, False, False),    # config 2 at 8 ranks: K = 1792 / 3584, NCCL measured faster
+    (8, 28672, False, True),     # config 5 at 8 ranks: y K = 3584 stays on NCCL, dx K = 7168 fuses
+])
+def test_fused_reduce_scatter_crossover(world, H, y_fused, dx_fused):
+    """The per-GEMM choice between the GEMM-fused reduce-scatter and NCCL:
+    fused once K >= 4333 (t - 1) / t (y: K = H / t, dx: K = 2H / t)."""
+    class Rule(tp.FusedReduceScatter):
+        def __init__(self, w):  # the rule only, no process group
+            self.world = w
+
+    r = Rule(world)
+    assert r.wants(H // world) == y_fused
+    assert r.wants(2 * H // world) == dx_fused
