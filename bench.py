@@ -668,6 +668,109 @@ def run_ours_single(args):
     return line
 
 
+def run_ours_tp(args):
+    """Strong-scaling tensor-parallel run of one block of the workload's shape
+    on WORLD_SIZE GPUs (one process per GPU, swiglu_b200.tp). Returns the JSON
+    dict on rank 0, None elsewhere."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from swiglu_b200 import ops
+    from swiglu_b200.tp import FusedReduceScatter, SwiGLUMLPTensorParallel
+
+    cfg, metric, workload = WORKLOADS[args.workload]
+    data = "synthetic" if cfg is CFG else "synthetic, drawn on the device"
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+    try:
+        M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
+        assert M % world == 0 and H % world == 0
+        x, w1, w2, gy = _inputs(dev, cfg=cfg)
+        ms_rows = M // world
+        fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
+        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
+                                        fused_rs=None if fused else False).to(dev).load_full(w1, w2)
+        params = list(model.parameters())
+        x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
+        gy_l = gy[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
+        del x, w1, w2, gy
+
+        def step():
+            xi = x_l.detach().requires_grad_(True)
+            y = model(xi)
+            return torch.autograd.grad(y, [xi] + params, gy_l)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            time.sleep(0.3)
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(st)
+            for _ in range(args.steps):
+                step()
+            e1.record(st)
+            torch.cuda.synchronize()
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+
+        # End to end with host buffers: this rank's token shard in from pinned
+        # host memory and its grad_x out, on a copy stream one step ahead of
+        # the compute (the single-GPU bench's pipelined loop), max over ranks.
+        x_host, gy_host = x_l.cpu(), gy_l.cpu()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2e_ms, h2d, d2h = e2e_pipelined(model, params, x_host, gy_host, dev, args)
+        e2e_ms = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        e2e_ms = e2e_ms.item()
+        status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
+        dist.all_reduce(status, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        # This library's launches per rank and step: GEMM1, y, grad_h, dW2, dW1,
+        # dx, plus a signal and an owner-reduce kernel for each GEMM that
+        # carries its reduce-scatter (y with K = H/t, dx with K = 2H/t).
+        frs = model.fused_rs if isinstance(model.fused_rs, FusedReduceScatter) else None
+        launches = 6 + (2 * sum(frs.wants(k) for k in (H // world, 2 * H // world)) if frs else 0)
+        if rank != 0:
+            return None
+        fl = flops_fwd_bwd(M, D, H, Dout)
+        peaks, src = load_peaks()
+        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        value = fl / (ms * 1e-3) / 1e12
+        return {
+            "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": data,
+            "config": {"workload": workload + ", tensor parallel", **cfg,
+                       "parallelism": f"tp{world}",
+                       "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
+                                  if fused else "f32 partials, NCCL reduce-scatter"),
+                       "l2": "working set > L2"},
+            "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches * args.steps * world,
+            "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
+            "device_status": int(status.item()),
+            "clocks": clk.summary(),
+        }
+    finally:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -719,12 +822,7 @@ def main():
         line = run_ours_single(args)
         print(json.dumps(line), flush=True)
         return
-    from swiglu_b200 import tp
-    cfg, metric, workload = WORKLOADS[args.workload]
-    line = tp.bench_tp(args, cfg, flops_fwd_bwd, metric, ClockSampler, load_peaks, cpu_reference_sample,
-                       e2e_pipelined, workload=workload,
-                       inputs_fn=lambda dev: _inputs(dev, cfg=cfg),
-                       data="synthetic" if cfg is CFG else "synthetic, drawn on the device")
+    line = run_ours_tp(args)
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -141,67 +141,3 @@ class SwiGLUMLPFused(nn.Module):
 
     def forward(self, x):
         return SwiGLUFusedForwardFunction.apply(x, self.w1t, self.w2)
-
-
-# -----------------------------------------------------------------------------
-# Self-test: fused vs ground truth (fp32 + bf16), plus preact/h sanity
-# (same checks and tolerances as fused_forward.py:311-371).
-# -----------------------------------------------------------------------------
-def _selftest():
-    import torch.nn.functional as F
-    from swiglu_recompute import SwiGLUMLPGroundTruth
-
-    assert torch.cuda.is_available(), "needs a CUDA GPU"
-    torch.cuda.set_device(0)
-    print(f"torch {torch.__version__} | {torch.cuda.get_device_name(0)}")
-
-    D, H, Dout = 3584, 14336, 3584
-    M = 512
-
-    def run(dtype, tol):
-        torch.manual_seed(0)
-        gt = SwiGLUMLPGroundTruth(D, H, Dout, dtype=dtype).cuda()
-        fused = SwiGLUMLPFused(D, H, Dout, dtype=dtype).cuda()
-        with torch.no_grad():
-            fused.w1t.copy_(gt.w1.t().contiguous())
-            fused.w2.copy_(gt.w2)
-        x0 = torch.randn(M, D, device="cuda", dtype=dtype)
-        xg = x0.detach().clone().requires_grad_(True)
-        xf = x0.detach().clone().requires_grad_(True)
-        yg = gt(xg)
-        yf = fused(xf)
-        gout = torch.randn_like(yg)
-        gg = torch.autograd.grad(yg, [xg, gt.w1, gt.w2], gout)
-        gf = torch.autograd.grad(yf, [xf, fused.w1t, fused.w2], gout)
-
-        def rel(a, b):
-            denom = b.float().abs().max().clamp_min(1e-6)
-            return ((a.float() - b.float()).abs().max() / denom).item()
-
-        checks = {"out": rel(yf, yg), "grad_x": rel(gf[0], gg[0]),
-                  "grad_W1": rel(gf[1].t(), gg[1]), "grad_W2": rel(gf[2], gg[2])}
-        ok = all(v <= tol for v in checks.values())
-        print(f"  [{dtype}] tol={tol:g}")
-        for name, v in checks.items():
-            print(f"      {name:<9s} rel_max={v:.3e}  {'OK' if v <= tol else 'FAIL'}")
-        print(f"  => {'PASS' if ok else 'FAIL'}")
-        return ok
-
-    torch.manual_seed(1)
-    wt = torch.randn(D, 2 * H, device="cuda", dtype=torch.float32) * (D ** -0.5)
-    x = torch.randn(M, D, device="cuda", dtype=torch.float32) * (D ** -0.5)
-    preact, h = fused_matmul_swiglu_save_preact(x, wt)
-    ref_preact = x @ wt
-    left, gate = ref_preact.chunk(2, dim=-1)
-    ref_h = left * F.silu(gate)
-    print(f"  [sanity fp32] preact max_abs={(preact - ref_preact).abs().max().item():.3e}  "
-          f"h max_abs={(h - ref_h).abs().max().item():.3e}")
-
-    ok32 = run(torch.float32, tol=1e-4)
-    okbf = run(torch.bfloat16, tol=2e-2)
-    print("ALL PASS" if (ok32 and okbf) else "FAILURES PRESENT")
-    return ok32 and okbf
-
-
-if __name__ == "__main__":
-    _selftest()

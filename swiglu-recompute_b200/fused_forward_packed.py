@@ -224,54 +224,3 @@ class SwiGLUMLPPackedFused(nn.Module):
 
     def forward(self, x):
         return SwiGLUPackedFusedFunction.apply(x, self.packed_weight, self.w2)
-
-
-# -----------------------------------------------------------------------------
-# Self-test vs ground truth (fp32 + bf16), as fused_forward_packed.py:342-383.
-# -----------------------------------------------------------------------------
-def _selftest():
-    from swiglu_recompute import SwiGLUMLPGroundTruth
-
-    assert torch.cuda.is_available()
-    torch.cuda.set_device(0)
-    print(f"torch {torch.__version__} | {torch.cuda.get_device_name(0)}")
-    D, H, Dout, M = 3584, 14336, 3584, 512
-
-    def run(dtype, tol):
-        torch.manual_seed(0)
-        gt = SwiGLUMLPGroundTruth(D, H, Dout, dtype=dtype).cuda()
-        pk = SwiGLUMLPPackedFused(D, H, Dout, dtype=dtype).cuda()
-        with torch.no_grad():
-            pk.packed_weight.copy_(pack_swiglu_linear_weight(gt.w1.contiguous()))
-            pk.w2.copy_(gt.w2)
-        x0 = torch.randn(M, D, device="cuda", dtype=dtype)
-        xg = x0.detach().clone().requires_grad_(True)
-        xp = x0.detach().clone().requires_grad_(True)
-        yg = gt(xg)
-        yp = pk(xp)
-        gout = torch.randn_like(yg)
-        gg = torch.autograd.grad(yg, [xg, gt.w1, gt.w2], gout)
-        gp = torch.autograd.grad(yp, [xp, pk.packed_weight, pk.w2], gout)
-
-        def rel(a, b):
-            return ((a.float() - b.float()).abs().max()
-                    / b.float().abs().max().clamp_min(1e-6)).item()
-
-        grad_w1 = unpack_swiglu_linear_weight(gp[1])
-        checks = {"out": rel(yp, yg), "grad_x": rel(gp[0], gg[0]),
-                  "grad_W1": rel(grad_w1, gg[1]), "grad_W2": rel(gp[2], gg[2])}
-        ok = all(v <= tol for v in checks.values())
-        print(f"  [{dtype}] tol={tol:g}")
-        for n, v in checks.items():
-            print(f"      {n:<9s} rel_max={v:.3e}  {'OK' if v <= tol else 'FAIL'}")
-        print(f"  => {'PASS' if ok else 'FAIL'}")
-        return ok
-
-    ok32 = run(torch.float32, tol=1e-4)
-    okbf = run(torch.bfloat16, tol=2e-2)
-    print("ALL PASS" if (ok32 and okbf) else "FAILURES PRESENT")
-    return ok32 and okbf
-
-
-if __name__ == "__main__":
-    _selftest()

@@ -91,47 +91,3 @@ class SwiGLUMLPPackedFusedCanon(nn.Module):
 
     def forward(self, x):
         return SwiGLUPackedFusedFunctionCanon.apply(x, self.packed_weight, self.w2)
-
-
-def _selftest():
-    from swiglu_recompute import SwiGLUMLPGroundTruth
-
-    assert torch.cuda.is_available()
-    torch.cuda.set_device(0)
-    D, H, Dout, M = 3584, 14336, 3584, 512
-
-    def run(dtype, tol):
-        torch.manual_seed(0)
-        gt = SwiGLUMLPGroundTruth(D, H, Dout, dtype=dtype).cuda()
-        pk = SwiGLUMLPPackedFusedCanon(D, H, Dout, dtype=dtype).cuda()
-        with torch.no_grad():
-            pk.packed_weight.copy_(pack_swiglu_linear_weight(gt.w1.contiguous()))
-            pk.w2.copy_(gt.w2)
-        x0 = torch.randn(M, D, device="cuda", dtype=dtype)
-        xg = x0.detach().clone().requires_grad_(True)
-        xp = x0.detach().clone().requires_grad_(True)
-        yg = gt(xg)
-        yp = pk(xp)
-        gout = torch.randn_like(yg)
-        gg = torch.autograd.grad(yg, [xg, gt.w1, gt.w2], gout)
-        gp = torch.autograd.grad(yp, [xp, pk.packed_weight, pk.w2], gout)
-
-        def rel(a, b):
-            return ((a.float() - b.float()).abs().max()
-                    / b.float().abs().max().clamp_min(1e-6)).item()
-
-        checks = {"out": rel(yp, yg), "grad_x": rel(gp[0], gg[0]),
-                  "grad_W1": rel(unpack_swiglu_linear_weight(gp[1]), gg[1]),
-                  "grad_W2": rel(gp[2], gg[2])}
-        ok = all(v <= tol for v in checks.values())
-        print(f"  [{dtype}] " + "  ".join(f"{n}={v:.3e}" for n, v in checks.items())
-              + ("  PASS" if ok else "  FAIL"))
-        return ok
-
-    ok = run(torch.float32, 1e-4) and run(torch.bfloat16, 2e-2)
-    print("ALL PASS" if ok else "FAILURES PRESENT")
-    return ok
-
-
-if __name__ == "__main__":
-    _selftest()

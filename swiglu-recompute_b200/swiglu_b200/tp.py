@@ -10,8 +10,10 @@ Tokens are sharded along M: each rank holds x_r [M/t, D] and y_r [M/t, Dout].
 forward   x = all_gather(x_r) ; preact_r, h_r = GEMM1+SwiGLU(x, W1_r)
           y_partial = h_r . W2_r^T (f32) ; y_r = reduce_scatter(y_partial)
 backward  grad_y = all_gather(grad_y_r)
-          dW2_r = grad_y^T . h_r (h recomputed in the GEMM prologue)
           preact_r <- grad_preact_r (in place) ; dW1_r = grad_preact_r^T . x
+          dW2_r = grad_y^T . h_r, h_r recomputed from preact_r as the
+          single-GPU backward does (ops.dw2_mode: inside the dW2 kernel's
+          operand prologue, or written by the grad_preact epilogue)
           dx_partial = grad_preact_r . W1_r (f32) ; dx_r = reduce_scatter(dx_partial)
 Partials are reduced in f32 and rounded once, so the result does not depend
 on how many bf16 hops a ring reduction takes.
@@ -23,9 +25,6 @@ SwiGLUMemoryOptimizedFunction, swiglu_recompute.py:58-78).
 from __future__ import annotations
 
 import ctypes
-import os
-import time
-from datetime import timedelta
 
 import torch
 import torch.distributed as dist
@@ -307,104 +306,3 @@ class SwiGLUMLPTensorParallel(nn.Module):
                 self.fused_rs = FusedReduceScatter(self.group)
             frs = self.fused_rs
         return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32, frs)
-
-
-# -------------------------------------------------------------- bench
-def bench_tp(args, cfg, flops_fn, metric, clock_cls, load_peaks, cpu_sample, e2e_fn, *,
-             workload="cfg2: one SwiGLU MLP block fwd+bwd", inputs_fn=None, data="synthetic"):
-    """Strong-scaling TP run of one block of shape `cfg` on WORLD_SIZE GPUs (one
-    process per GPU). `inputs_fn(device)` draws (x, W1, W2, grad_y) (default:
-    on the host). Returns the JSON dict on rank 0, None elsewhere."""
-    from swiglu_b200.synthetic import make_inputs
-
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", str(rank)))
-    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
-    try:
-        M, D, H, Dout = cfg["M"], cfg["D"], cfg["H"], cfg["Dout"]
-        assert M % world == 0 and H % world == 0
-        if inputs_fn is None:
-            x, w1, w2, gy = make_inputs(M, D, H, Dout, seed=0, dtype=torch.bfloat16)
-        else:
-            x, w1, w2, gy = inputs_fn(dev)
-        ms_rows = M // world
-        fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
-        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
-                                        fused_rs=None if fused else False).to(dev).load_full(w1, w2)
-        params = list(model.parameters())
-        x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
-        gy_l = gy[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
-        del x, w1, w2, gy
-
-        def step():
-            xi = x_l.detach().requires_grad_(True)
-            y = model(xi)
-            return torch.autograd.grad(y, [xi] + params, gy_l)
-
-        for _ in range(args.warmup):
-            step()
-        torch.cuda.synchronize()
-        st = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with clock_cls(local) as clk:
-            time.sleep(0.3)
-            dist.barrier()
-            torch.cuda.synchronize()
-            e0.record(st)
-            for _ in range(args.steps):
-                step()
-            e1.record(st)
-            torch.cuda.synchronize()
-            dist.barrier()
-        ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        ms = ms.item()
-
-        # End to end with host buffers: this rank's token shard in from pinned
-        # host memory and its grad_x out, on a copy stream one step ahead of
-        # the compute (the single-GPU bench's pipelined loop), max over ranks.
-        x_host, gy_host = x_l.cpu(), gy_l.cpu()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e2e_ms, h2d, d2h = e2e_fn(model, params, x_host, gy_host, dev, args)
-        e2e_ms = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-        e2e_ms = e2e_ms.item()
-        status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
-        dist.all_reduce(status, op=dist.ReduceOp.MAX)
-        dist.barrier()
-        # This library's launches per rank and step: GEMM1, y, grad_h, dW2, dW1,
-        # dx, plus a signal and an owner-reduce kernel for each GEMM that
-        # carries its reduce-scatter (y with K = H/t, dx with K = 2H/t).
-        frs = model.fused_rs if isinstance(model.fused_rs, FusedReduceScatter) else None
-        launches = 6 + (2 * sum(frs.wants(k) for k in (H // world, 2 * H // world)) if frs else 0)
-        if rank != 0:
-            return None
-        fl = flops_fn(M, D, H, Dout)
-        peaks, src = load_peaks()
-        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-        value = fl / (ms * 1e-3) / 1e12
-        return {
-            "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": data,
-            "config": {"workload": workload + ", tensor parallel", **cfg,
-                       "parallelism": f"tp{world}",
-                       "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
-                                  if fused else "f32 partials, NCCL reduce-scatter"),
-                       "l2": "working set > L2"},
-            "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                    "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
-            "gpu_launches": launches * args.steps * world,
-            "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
-            "device_status": int(status.item()),
-            "clocks": clk.summary(),
-        }
-    finally:
-        dist.destroy_process_group()
