@@ -16,6 +16,8 @@ tests/test_oracle_golden.py).
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 STD, PACKED = "std", "packed"
@@ -28,8 +30,14 @@ def rel_max(a: torch.Tensor, b: torch.Tensor) -> float:
     return ((a.float() - b.float()).abs().max() / denom).item()
 
 
+def _wide(t: torch.Tensor) -> torch.Tensor:
+    """f32 for the arithmetic, unless the caller works in f64 already."""
+    return t if t.dtype == torch.float64 else t.float()
+
+
 def _bf16(t: torch.Tensor) -> torch.Tensor:
-    return t.to(torch.bfloat16).to(torch.float32)
+    """Round to bf16 and return in the working precision (f32, or f64)."""
+    return t.to(torch.bfloat16).to(torch.float64 if t.dtype == torch.float64 else torch.float32)
 
 
 def _round(t: torch.Tensor, bf16: bool) -> torch.Tensor:
@@ -72,7 +80,7 @@ def forward_logic(preact: torch.Tensor, layout: str = STD, bf16: bool = False) -
     fused_forward_packed.py:281-286). f32 math, one rounding."""
     H = preact.shape[-1] // 2
     li, gi = col_index(H, layout)
-    p = preact.float()
+    p = _wide(preact)
     left, gate = p[:, li], p[:, gi]
     return _round(left * (gate * torch.sigmoid(gate)), bf16)
 
@@ -83,9 +91,9 @@ def backward_logic(preact: torch.Tensor, grad_h: torch.Tensor, layout: str = STD
     packed: fused_forward_packed.py:247-259)."""
     H = preact.shape[-1] // 2
     li, gi = col_index(H, layout)
-    p = preact.float()
+    p = _wide(preact)
     left, gate = p[:, li], p[:, gi]
-    g = grad_h.float()
+    g = _wide(grad_h).to(p.dtype)
     sig = torch.sigmoid(gate)
     silu = gate * sig
     dsilu = sig + silu * (1.0 - sig)
@@ -120,20 +128,54 @@ def mlp_forward_backward(x, w1_rows, w2, grad_y, *, bf16: bool = False,
     return {"y": y, "dx": dx, "dw1": dw1, "dw2": dw2, "preact": preact, "h": h}
 
 
-def reference_path_bf16(x, w1_rows, w2, grad_y):
-    """The recompute Function's own bf16 arithmetic, op for op
-    (swiglu_recompute.py:58-78): bf16 x bf16 -> bf16 matmuls (f32
-    accumulation in the BLAS of whatever device the tensors live on) and the
-    pointwise helpers in f32 rounded once. Run on CUDA tensors it reproduces
-    what the reference computes on the GPU; the parity tests use it there."""
+def reference_path_bf16(x, w1_rows, w2, grad_y, *, h_from_accumulator: bool = False):
+    """The reference's own bf16 arithmetic, op for op: bf16 x bf16 -> bf16
+    matmuls (f32 accumulation in the BLAS of whatever device the tensors live
+    on) and the pointwise helpers in f32 rounded once. Run on CUDA tensors it
+    reproduces what the reference computes on the GPU; the parity tests use it
+    there.
+
+    Default: the recompute Function (swiglu_recompute.py:58-78), h from the
+    bf16 preact. h_from_accumulator: the fused forward kernels
+    (fused_forward.py:165-185, fused_forward_packed.py:167-183), which form h
+    from the f32 accumulator of x . W1^T before preact is rounded; their
+    backward is the recompute backward (fused_forward.py:277-284,
+    fused_forward_packed.py:303-316)."""
     x, w1, w2, gy = (t.to(torch.bfloat16) for t in (x, w1_rows, w2, grad_y))
-    preact = x @ w1.t()
-    h = forward_logic(preact.float(), STD, True).to(torch.bfloat16)
+    if h_from_accumulator:
+        acc = x.float() @ w1.float().t()
+        preact = acc.to(torch.bfloat16)
+        h = forward_logic(acc, STD, True).to(torch.bfloat16)
+    else:
+        preact = x @ w1.t()
+        h = forward_logic(preact.float(), STD, True).to(torch.bfloat16)
     y = h @ w2.t()
-    dw2 = gy.t() @ h
+    h_bwd = forward_logic(preact.float(), STD, True).to(torch.bfloat16)
+    dw2 = gy.t() @ h_bwd
     grad_h = gy @ w2
     gp = backward_logic(preact.float(), grad_h.float(), STD, True).to(torch.bfloat16)
     return {"y": y, "dx": gp @ w1, "dw1": gp.t() @ x, "dw2": dw2}
+
+
+def bf16_resolution(ref: torch.Tensor) -> float:
+    """One bf16 ulp of the largest |element| of `ref`, relative to it: the
+    smallest non-zero rel_max that two bf16 results can have when the
+    largest element itself differs by a rounding flip (between 2^-8 and 2^-7)."""
+    m = ref.double().abs().max().item()
+    if m == 0.0:
+        return 0.0
+    return 2.0 ** (math.floor(math.log2(m)) - 7) / m
+
+
+def bf16_ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Per-element distance between two bf16-valued tensors in units in the
+    last place: how many representable bf16 values lie between them (+0 and
+    -0 coincide). Both inputs are cast to bf16 first (exact for bf16 values)."""
+    def line(t):
+        i = t.to(torch.bfloat16).contiguous().view(torch.int16).to(torch.int32)
+        mag = i & 0x7FFF
+        return torch.where(i < 0, -mag, mag)
+    return (line(a) - line(b)).abs()
 
 
 def ground_truth(x, w1, w2, grad_y):

@@ -329,4 +329,27 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
+// The hardware tanh approximation (tanh.approx.f32, one MUFU operation).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// h = left * silu(gate) for a pair of bf16 elements, rounded to bf16, with
+// silu(g) = g * sigmoid(g) and sigmoid(g) = (1 + tanh(g / 2)) / 2, i.e.
+// silu(g) = g/2 + (g/2) tanh(g/2): one MUFU operation per element (against an
+// exp and a reciprocal for sigmoid_fast) and the f32 arithmetic on packed
+// f32x2 instructions. Used where h is recomputed many times per element (the
+// dW2 operand prologue), so the special-function unit is the limit there.
+__device__ __forceinline__ uint32_t swiglu_bf16x2_tanh(uint32_t left, uint32_t gate) {
+  const float2 l = unpack_bf16x2(left);
+  const float2 g = unpack_bf16x2(gate);
+  const float2 hg = __fmul2_rn(g, make_float2(0.5f, 0.5f));
+  const float2 t = make_float2(tanh_approx(hg.x), tanh_approx(hg.y));
+  const float2 silu = __ffma2_rn(hg, t, hg);
+  const float2 h = __fmul2_rn(l, silu);
+  return pack_bf16x2(h.x, h.y);
+}
+
 }  // namespace swiglu

@@ -238,11 +238,7 @@ __global__ void __launch_bounds__(Dw2Cfg::NUM_THREADS, 1) dw2_hprologue_kernel(c
           const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
           uint32_t hw[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 l2 = unpack_bf16x2(lw[e]);
-            const float2 g2 = unpack_bf16x2(gw[e]);
-            hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
-          }
+          for (int e = 0; e < 4; ++e) hw[e] = swiglu_bf16x2_tanh(lw[e], gw[e]);
           sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         }
         fence_proxy_async_smem();
@@ -520,11 +516,7 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
             const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
             uint32_t hw[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 l2 = unpack_bf16x2(lw[e]);
-              const float2 g2 = unpack_bf16x2(gw[e]);
-              hw[e] = pack_bf16x2(l2.x * (g2.x * sigmoid_fast(g2.x)), l2.y * (g2.y * sigmoid_fast(g2.y)));
-            }
+            for (int e = 0; e < 4; ++e) hw[e] = swiglu_bf16x2_tanh(lw[e], gw[e]);
             sa[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
           }
           fence_proxy_async_smem();

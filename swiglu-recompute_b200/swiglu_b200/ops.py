@@ -89,6 +89,33 @@ def set_stream_k(enabled: bool) -> None:
         _workspaces.clear()
 
 
+# Launch trace: with a list installed by trace_launches(), every kernel entry
+# point called through this module also records a CUDA event before and after
+# its launch on the launching stream and appends (entry point, start, end).
+# The events cost no device time worth measuring, so a caller (bench.py) can
+# time each kernel inside the very steps it times as a whole.
+_trace: list | None = None
+
+
+def trace_launches(records: list | None) -> None:
+    """Install `records` (a list) to collect (entry point, start event, end
+    event) per launch from now on; None stops tracing."""
+    global _trace
+    _trace = records
+
+
+def _call(dev: torch.device, name: str, *args) -> None:
+    if _trace is None:
+        _lib.call(name, *args)
+        return
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    _lib.call(name, *args)
+    e1.record(st)
+    _trace.append((name, e0, e1))
+
+
 def _check_cuda(*ts: torch.Tensor) -> torch.device:
     dev = None
     for t in ts:
@@ -135,9 +162,9 @@ def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
     preact = torch.empty((M, n2), device=dev, dtype=dt) if want_preact else None
     h = torch.empty((M, H), device=dev, dtype=dt) if want_h else None
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_fused_matmul_swiglu_save_preact", _p(x), _p(w), _p(preact), _p(h),
-                  M, K, H, dtype_code(dt), w_form, layout, int(bool(h_from_rounded)),
-                  int(group_size_m), _stream(dev))
+        _call(dev, "swiglu_b200_fused_matmul_swiglu_save_preact", _p(x), _p(w), _p(preact), _p(h),
+              M, K, H, dtype_code(dt), w_form, layout, int(bool(h_from_rounded)),
+              int(group_size_m), _stream(dev))
     return preact, h
 
 
@@ -158,8 +185,8 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, a_t: bool, b_t: bool,
     else:
         assert out.shape == (M, N) and out.dtype == odt
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_matmul_tiled", _p(a), _p(b), _p(out), M, N, K, int(a_t), int(b_t),
-                  dtype_code(dt), dtype_code(odt), int(group_size_m), int(tile_n), _stream(dev))
+        _call(dev, "swiglu_b200_matmul_tiled", _p(a), _p(b), _p(out), M, N, K, int(a_t), int(b_t),
+              dtype_code(dt), dtype_code(odt), int(group_size_m), int(tile_n), _stream(dev))
     return out
 
 
@@ -175,8 +202,8 @@ def bwd_dw2(grad_y: torch.Tensor, preact: torch.Tensor, *, layout: int,
     if out is None:
         out = torch.empty((Dout, H), device=dev, dtype=dt)
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_bwd_dw2", _p(grad_y), _p(preact), _p(out), M, H, Dout,
-                  dtype_code(dt), layout, _stream(dev))
+        _call(dev, "swiglu_b200_bwd_dw2", _p(grad_y), _p(preact), _p(out), M, H, Dout,
+              dtype_code(dt), layout, _stream(dev))
     return out
 
 
@@ -192,12 +219,12 @@ def bwd_grad_preact_inplace(grad_y: torch.Tensor, w2: torch.Tensor, preact: torc
     assert Dout == Dout2 and preact.shape == (M, 2 * H)
     with torch.cuda.device(dev):
         if h_out is None:
-            _lib.call("swiglu_b200_bwd_grad_preact_inplace", _p(grad_y), _p(w2), _p(preact), M, H, Dout,
-                      dtype_code(dt), layout, _stream(dev))
+            _call(dev, "swiglu_b200_bwd_grad_preact_inplace", _p(grad_y), _p(w2), _p(preact), M, H, Dout,
+                  dtype_code(dt), layout, _stream(dev))
         else:
             assert h_out.shape == (M, H)
-            _lib.call("swiglu_b200_bwd_grad_preact_inplace_emit_h", _p(grad_y), _p(w2), _p(preact),
-                      _p(h_out), M, H, Dout, dtype_code(dt), layout, _stream(dev))
+            _call(dev, "swiglu_b200_bwd_grad_preact_inplace_emit_h", _p(grad_y), _p(w2), _p(preact),
+                  _p(h_out), M, H, Dout, dtype_code(dt), layout, _stream(dev))
     return preact
 
 
@@ -208,8 +235,8 @@ def forward_logic(preact: torch.Tensor, *, layout: int) -> torch.Tensor:
     H = n2 // 2
     h = torch.empty((M, H), device=dev, dtype=preact.dtype)
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_forward_logic", _p(preact), _p(h), M, H, dtype_code(preact.dtype),
-                  layout, _stream(dev))
+        _call(dev, "swiglu_b200_forward_logic", _p(preact), _p(h), M, H, dtype_code(preact.dtype),
+              layout, _stream(dev))
     return h
 
 
@@ -223,8 +250,8 @@ def backward_logic(preact: torch.Tensor, grad_h: torch.Tensor, *, layout: int,
     if out is None:
         out = torch.empty_like(preact)
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_backward_logic", _p(preact), _p(grad_h), _p(out), M, H, dtype_code(dt),
-                  layout, _stream(dev))
+        _call(dev, "swiglu_b200_backward_logic", _p(preact), _p(grad_h), _p(out), M, H, dtype_code(dt),
+              layout, _stream(dev))
     return out
 
 
@@ -233,8 +260,8 @@ def pack_chunked(w: torch.Tensor, block_n_half: int, *, unpack: bool) -> torch.T
     K, n2 = w.shape
     out = torch.empty_like(w)
     with torch.cuda.device(dev):
-        _lib.call("swiglu_b200_pack_weight_chunked", _p(w), _p(out), K, n2 // 2, int(block_n_half),
-                  dtype_code(w.dtype), int(bool(unpack)), _stream(dev))
+        _call(dev, "swiglu_b200_pack_weight_chunked", _p(w), _p(out), K, n2 // 2, int(block_n_half),
+              dtype_code(w.dtype), int(bool(unpack)), _stream(dev))
     return out
 
 

@@ -7,8 +7,13 @@ inputs, and every output (y, dx, dW1, dW2) is compared, as rel_max
 
   exact   the f32 ground truth of the same (bf16-valued) inputs
           bound: bf16 7e-3, fp32 1e-5
-  refgpu  the recompute Function's own bf16 arithmetic run on the same GPU
-          (cuBLAS bf16 GEMMs, f32 pointwise): bound bf16 7e-3
+  refgpu  the reference's own bf16 arithmetic run on the same GPU (cuBLAS
+          bf16 GEMMs, f32 pointwise): the recompute Function's for the
+          recompute variant, h from the f32 accumulator for the fused,
+          packed and canon variants (as their Triton forward kernels form
+          it); bound bf16 7e-3 for every variant (or one bf16 ulp of the
+          largest element, 2^-8 .. 2^-7 of it, where that is more: the
+          smallest difference a single rounding flip there makes)
   oracle  the CPU restatement with the reference's rounding points
           bound: bf16 1e-2, fp32 1e-5
 
@@ -38,14 +43,15 @@ REFGPU_TOL = 7e-3
 TOL = ORACLE_TOL
 
 
-def check_all(out, x, w1, w2, gy, dtype, *, h_from_accumulator=False, refgpu=True):
+def check_all(out, x, w1, w2, gy, dtype, *, h_from_accumulator=False):
     bf = dtype == torch.bfloat16
     ref = O.mlp_forward_backward(x, w1, w2, gy, bf16=bf, h_from_accumulator=h_from_accumulator)
     gt = O.ground_truth(x.float(), w1.float(), w2.float(), gy.float())
     rg = None
-    if bf and refgpu:
+    if bf:
         rg = {k: v.float().cpu() for k, v in
-              O.reference_path_bf16(x.cuda(), w1.cuda(), w2.cuda(), gy.cuda()).items()}
+              O.reference_path_bf16(x.cuda(), w1.cuda(), w2.cuda(), gy.cuda(),
+                                    h_from_accumulator=h_from_accumulator).items()}
     for k in ("y", "dx", "dw1", "dw2"):
         e_gt, e_or = O.rel_max(out[k], gt[k]), O.rel_max(out[k], ref[k])
         # At small shapes the reference's own bf16 arithmetic can already sit
@@ -55,8 +61,14 @@ def check_all(out, x, w1, w2, gy, dtype, *, h_from_accumulator=False, refgpu=Tru
         assert e_gt <= bound, (k, "exact", e_gt, bound)
         assert e_or <= ORACLE_TOL[dtype], (k, "oracle", e_or)
         if rg is not None:
+            # 7e-3, or one bf16 ulp of the largest element where that is more:
+            # two bf16 results whose f32 sums differ in order alone flip a
+            # rounding now and then, and a flip at the largest element is
+            # 2^-8 .. 2^-7 of it (measured: 7.35e-3 in dx of the fused
+            # variant at M=512 D=1024 H=2816, one flip at an element of 1.06).
             e_rg = O.rel_max(out[k], rg[k])
-            assert e_rg <= REFGPU_TOL, (k, "refgpu", e_rg)
+            bound_rg = max(REFGPU_TOL, O.bf16_resolution(rg[k]))
+            assert e_rg <= bound_rg, (k, "refgpu", e_rg, bound_rg)
 VARIANTS = ["recompute", "fused", "packed", "canon"]
 
 
@@ -106,8 +118,7 @@ def run_variant(variant, M, D, H, Dout, dtype, seed=0):
 ])
 def test_variant_matches_oracle(variant, dtype, M, D, H, Dout):
     (x, w1, w2, gy), out = run_variant(variant, M, D, H, Dout, dtype)
-    fused = variant != "recompute"
-    check_all(out, x, w1, w2, gy, dtype, h_from_accumulator=fused, refgpu=not fused)
+    check_all(out, x, w1, w2, gy, dtype, h_from_accumulator=variant != "recompute")
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
@@ -123,8 +134,7 @@ def test_config1_shape_recompute(dtype):
 def test_reference_selftest_shape_bf16(variant):
     # The reference self-test shape (fused_forward.py:320-321): D=3584 H=14336 M=512.
     (x, w1, w2, gy), out = run_variant(variant, 512, 3584, 14336, 3584, torch.bfloat16, seed=0)
-    fused = variant != "recompute"
-    check_all(out, x, w1, w2, gy, torch.bfloat16, h_from_accumulator=fused, refgpu=not fused)
+    check_all(out, x, w1, w2, gy, torch.bfloat16, h_from_accumulator=variant != "recompute")
 
 
 def test_ragged_shapes_recompute():

@@ -32,27 +32,32 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def _existing_pipeline(a, b, M, N, K):
+def _code(dtype):
+    return _lib.F32 if dtype == torch.float32 else _lib.BF16
+
+
+def _existing_pipeline(a, b, M, N, K, out_dtype=torch.bfloat16):
     """The same computation through the existing entry points, with a
     caller-allocated receive buffer and flag array (world = 1)."""
     lib = _lib.load()
     recv = torch.empty(M * N, dtype=torch.float32, device="cuda")
     flags = torch.zeros(1, dtype=torch.int32, device="cuda")
-    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(M, N, dtype=out_dtype, device="cuda")
     peers = (ctypes.c_void_p * 1)(recv.data_ptr())
     peer_flags = (ctypes.c_void_p * 1)(flags.data_ptr())
     _lib.check(lib.swiglu_b200_matmul_scatter_rows(_p(a), _p(b), M, N, K, 0, 1, _lib.BF16, peers, 1, 0, M,
                                                    _stream()))
     _lib.check(lib.swiglu_b200_tp_signal(peer_flags, 1, 0, 7, _stream()))
-    _lib.check(lib.swiglu_b200_tp_reduce_rows(_p(recv), _p(flags), 1, 7, _p(out), M, N, _lib.BF16, _stream()))
+    _lib.check(lib.swiglu_b200_tp_reduce_rows(_p(recv), _p(flags), 1, 7, _p(out), M, N, _code(out_dtype),
+                                              _stream()))
     return out
 
 
-def _noalloc(a, b, M, N, K):
+def _noalloc(a, b, M, N, K, out_dtype=torch.bfloat16):
     lib = _lib.load()
-    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    _lib.check(lib.swiglu_b200_matmul_reduce_rows_noalloc(_p(a), _p(b), _p(out), M, N, K, 0, 1, _lib.BF16,
-                                                          _stream()))
+    out = torch.empty(M, N, dtype=out_dtype, device="cuda")
+    _lib.check(lib.swiglu_b200_matmul_reduce_rows_noalloc(_p(a), _p(b), _p(out), M, N, K, 0, 1,
+                                                          _code(out_dtype), _stream()))
     return out
 
 
@@ -69,6 +74,29 @@ def test_noalloc_matches_existing_entry_points_twice_in_a_row():
         assert O.rel_max(got.cpu(), want.cpu()) <= BF16_TOL
         exact = a.float().cpu() @ b.float().cpu().t()
         assert O.rel_max(got.cpu(), exact) <= BF16_TOL
+    assert _lib.device_status() == 0
+
+
+def test_noalloc_at_its_limit_and_with_f32_output():
+    """M * N exactly at the scratch size (every scratch float written), then
+    an f32 output twice in a row, each against the caller-buffer pipeline
+    (bit for bit: same kernels, same summation order) and the exact product."""
+    torch.cuda.set_device(0)
+    g = torch.Generator().manual_seed(22)
+    cases = [(4096, 1024, 256, torch.bfloat16, BF16_TOL),     # M * N == 4,194,304
+             (512, 768, 384, torch.float32, 1e-5),
+             (4096, 1024, 128, torch.float32, 1e-5)]
+    for M, N, K, odt, tol in cases:
+        a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+        b = (torch.randn(N, K, generator=g) * K ** -0.5).to(torch.bfloat16).cuda()
+        got = _noalloc(a, b, M, N, K, odt)
+        want = _existing_pipeline(a, b, M, N, K, odt)
+        torch.cuda.synchronize()
+        assert got.dtype == odt
+        assert torch.equal(got, want)
+        exact = a.float().cpu() @ b.float().cpu().t()
+        assert O.rel_max(got.float().cpu(), exact) <= tol
+    assert M * N == SCRATCH_FLOATS
     assert _lib.device_status() == 0
 
 
