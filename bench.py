@@ -10,9 +10,13 @@ inputs (x, grad_y ~ N(0,1); W ~ N(0, fan_in^-1/2)). FLOPs per step
 
   value      device-timed whole-job TFLOP/s, inputs resident in HBM (every
              step's working set, >= 1.5 GB, exceeds the 126 MB L2)
+  kernels_ms each native kernel's mean device time inside those same timed
+             steps (CUDA events around every launch on its stream)
   e2e        same metric through the public API with host buffers: pinned
              x and grad_y copied in and grad_x copied out every step
   roofline   the dominant kernel's algorithmic TFLOP/s vs measured bf16 peak
+  same_box   the reference's recompute algorithm (cuBLAS GEMMs + Inductor
+             pointwise) on the same GPU, burst and sustained, beside ours
   cpu_baseline  the reference's pure-PyTorch fp32 path (CPU restatement),
              timed on this host on a bounded row sample of the same shapes
 
@@ -184,50 +188,52 @@ def _inputs(dev, dtype=torch.bfloat16, cfg=CFG):
     return make_inputs(cfg["M"], cfg["D"], cfg["H"], cfg["Dout"], seed=0, dtype=dtype)
 
 
-def kernel_breakdown(x, w1, w2, gy, iters):
-    """Per-kernel device time of one fwd+bwd: CUDA events between the launches
-    on the launching stream, `iters` steps queued back to back (no host sync
-    in between, so the GPU never idles between kernels). {name: ms/launch}."""
-    from swiglu_b200 import ops
-    from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+def label_launches(names):
+    """Kernel names of the step's native launches, in launch order, from the
+    entry points the launch trace records (swiglu_b200.ops.trace_launches).
+    One step: GEMM1+SwiGLU, y; then either grad_h+dSwiGLU writing h and the
+    dW2 GEMM on it ("emit_h"), or the dW2 kernel with the h prologue and
+    grad_h+dSwiGLU ("prologue"); then dW1 and dx."""
+    out, fwd, dw2_pending, bwd_mm = [], True, False, 0
+    for n in names:
+        if n == "swiglu_b200_fused_matmul_swiglu_save_preact":
+            out.append("gemm1_swiglu")
+            fwd, dw2_pending, bwd_mm = True, False, 0
+        elif n == "swiglu_b200_bwd_dw2":
+            out.append("dw2_hprologue")
+            fwd = False
+        elif n in ("swiglu_b200_bwd_grad_preact_inplace_emit_h", "swiglu_b200_bwd_grad_preact_inplace"):
+            emit = n.endswith("emit_h")
+            out.append("gradh_dswiglu_emit_h" if emit else "gradh_dswiglu")
+            fwd, dw2_pending, bwd_mm = False, emit, 0
+        elif n == "swiglu_b200_matmul_tiled":
+            if fwd:
+                out.append("gemm2_y")
+            elif dw2_pending:
+                out.append("dw2_gemm")
+                dw2_pending = False
+            else:
+                out.append(("dw1", "dx")[min(bwd_mm, 1)])
+                bwd_mm += 1
+        else:
+            out.append(n)
+    return out
 
-    st = torch.cuda.current_stream()
-    names = ["gemm1_swiglu", "gemm2_y", "gradh_dswiglu_emit_h", "dw2_gemm", "dw1", "dx"]
-    evs = []
-    for _ in range(iters):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
-        ev[0].record(st)
-        preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
-        ev[1].record(st)
-        y = ops.matmul(h, w2, a_t=False, b_t=True)
-        ev[2].record(st)
-        del y
-        # the backward's order (swiglu_recompute._recompute_backward): grad_h
-        # GEMM writing grad_preact in place and h, then dW2 = grad_y^T h
-        ops.bwd_grad_preact_inplace(gy, w2, preact, layout=LAYOUT_STD, h_out=h)
-        ev[3].record(st)
-        dw2 = ops.matmul(gy, h, a_t=True, b_t=False)
-        ev[4].record(st)
-        del h
-        dw1 = ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512)
-        ev[5].record(st)
-        dx = ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512)
-        ev[6].record(st)
-        del preact, dw2, dw1, dx
-        evs.append(ev)
-    torch.cuda.synchronize()
-    acc = {n: 0.0 for n in names}
-    for ev in evs:
-        for i, n in enumerate(names):
-            acc[n] += ev[i].elapsed_time(ev[i + 1])
-    return {n: v / iters for n, v in acc.items()}
+
+def traced_kernel_ms(records, steps):
+    """{kernel: mean ms per step} of the launches recorded over `steps` steps."""
+    labels = label_launches([r[0] for r in records])
+    acc = {}
+    for lab, (_, e0, e1) in zip(labels, records):
+        acc[lab] = acc.get(lab, 0.0) + e0.elapsed_time(e1)
+    return {k: v / steps for k, v in acc.items()}
 
 
 def kernel_flops(M, D, H, Dout):
     g1 = 2.0 * M * D * 2 * H
     g2 = 2.0 * M * H * Dout
-    return {"gemm1_swiglu": g1, "gemm2_y": g2, "gradh_dswiglu_emit_h": g2, "dw2_gemm": g2,
-            "dw2_hprologue": g2, "dw1": g1, "dx": g1}
+    return {"gemm1_swiglu": g1, "gemm2_y": g2, "gradh_dswiglu_emit_h": g2, "gradh_dswiglu": g2,
+            "dw2_gemm": g2, "dw2_hprologue": g2, "dw1": g1, "dx": g1}
 
 
 def run_kernel_only(args):
@@ -551,6 +557,74 @@ def e2e_pipelined(model, params, x, gy, dev, args):
     return e0.elapsed_time(e1) / args.steps, x.numel() * 2 + gy.numel() * 2, M * D * 2
 
 
+def reference_recompute_module(D, H, Dout, w1, w2, dev):
+    """The reference's recompute MLP (swiglu_recompute.py:26-98) restated in
+    torch ops, for a same-GPU comparison arm: cuBLAS GEMMs in the
+    Function's order, and its two pointwise helpers compiled by Inductor as
+    the reference compiles them (@torch.compile, :26 and :33). Not the
+    reference's own file (it is not on the GPU box); the reference's Triton
+    fused forwards need their source and are not run."""
+    import torch.nn.functional as F
+
+    @torch.compile
+    def fwd_logic(preact):
+        left, gate = preact.chunk(2, dim=-1)
+        return left * F.silu(gate)
+
+    @torch.compile
+    def bwd_logic(preact, grad_h):
+        left, gate = preact.chunk(2, dim=-1)
+        sig = torch.sigmoid(gate)
+        silu = gate * sig
+        dsilu = sig + silu * (1.0 - sig)
+        return torch.cat([grad_h * silu, grad_h * left * dsilu], dim=-1)
+
+    class Fn(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, x, W1, W2):
+            preact = x @ W1.t()
+            ctx.save_for_backward(x, W1, W2, preact)
+            return fwd_logic(preact) @ W2.t()
+
+        @staticmethod
+        def backward(ctx, gy):
+            x, W1, W2, preact = ctx.saved_tensors
+            h = fwd_logic(preact)
+            gw2 = gy.t() @ h
+            gp = bwd_logic(preact, gy @ W2)
+            return gp @ W1, gp.t() @ x, gw2
+
+    class Module(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.w1 = torch.nn.Parameter(w1.to(dev, torch.bfloat16).clone())
+            self.w2 = torch.nn.Parameter(w2.to(dev, torch.bfloat16).clone())
+
+        def forward(self, x):
+            return Fn.apply(x, self.w1, self.w2)
+
+    return Module()
+
+
+def _timed_steps(step, steps, st):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _sustained_ms(step, steps, st, seconds, est_ms):
+    """ms per step over `steps` steps after `seconds` of back-to-back steps
+    (long enough for the 1 kW power cap to settle the clock)."""
+    for _ in range(max(1, int(seconds * 1e3 / est_ms))):
+        step()
+    return _timed_steps(step, steps, st)
+
+
 def run_ours_single(args):
     import swiglu_recompute as SR
     from swiglu_b200 import ops
@@ -567,45 +641,49 @@ def run_ours_single(args):
     params = list(model.parameters())
     xd, gyd = x.to(dev), gy.to(dev)
 
-    def step():
-        xi = xd.detach().requires_grad_(True)
-        y = model(xi)
-        return torch.autograd.grad(y, [xi] + params, gyd)
+    def make_step(mod, prm):
+        def step():
+            xi = xd.detach().requires_grad_(True)
+            y = mod(xi)
+            return torch.autograd.grad(y, [xi] + prm, gyd)
+        return step
 
+    step = make_step(model, params)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     assert ops.device_status(0) == 0, "kernel pipeline timeout during warm-up"
 
+    # The timed steps, with every native launch bracketed by CUDA events on
+    # its stream (ops.trace_launches): the per-kernel times below come from
+    # these very steps, at these steps' clocks.
     st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    records = []
     with ClockSampler(0) as clk:
         time.sleep(0.3)
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(args.steps):
-            step()
-        e1.record(st)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+        ops.trace_launches(records)
+        try:
+            ms = _timed_steps(step, args.steps, st)
+        finally:
+            ops.trace_launches(None)
     fl = flops_fwd_bwd(M, D, H, Dout)
     value = fl / (ms * 1e-3) / 1e12
+    kt = traced_kernel_ms(records, args.steps)
+    kf = kernel_flops(M, D, H, Dout)
+    dom = max(kt, key=kt.get)
+    launches = len(records)
+    del records
 
-    # The same step with dW2 in the "prologue" mode (h recomputed inside the
-    # dW2 kernel, no [M, H] buffer in backward), timed the same way.
-    ops.set_dw2_mode("prologue")
+    # The same step with dW2 in the other mode, timed the same way.
+    other = "emit_h" if ops.dw2_mode() == "prologue" else "prologue"
+    mode = ops.dw2_mode()
+    ops.set_dw2_mode(other)
     try:
         for _ in range(2):
             step()
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(args.steps):
-            step()
-        e1.record(st)
-        torch.cuda.synchronize()
-        ms_prologue = e0.elapsed_time(e1) / args.steps
+        ms_other = _timed_steps(step, args.steps, st)
     finally:
-        ops.set_dw2_mode("emit_h")
+        ops.set_dw2_mode(mode)
 
     # End to end through the public API with host buffers: every step copies
     # its x and grad_y in from pinned host memory and its grad_x out, on a copy
@@ -613,13 +691,8 @@ def run_ours_single(args):
     # step i move while step i+1 / i computes), as a data loader would.
     e2e_ms, h2d, d2h = e2e_pipelined(model, params, x.cpu(), gy.cpu(), dev, args)
 
-    # Per-kernel device times on the launching stream; dominant kernel roofline.
-    w1d, w2d = model.w1.detach(), model.w2.detach()
-    kt = kernel_breakdown(xd, w1d, w2d, gyd, iters=max(3, min(args.steps, 10)))
-    kf = kernel_flops(M, D, H, Dout)
-    dom = max(kt, key=kt.get)
     peaks, peak_src = load_peaks()
-    peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    burst, sustained = float(peaks["bf16_tflops"]), float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
     ach = kf[dom] / (kt[dom] * 1e-3) / 1e12
     assert ops.device_status(0) == 0, "kernel pipeline timeout"
 
@@ -629,35 +702,45 @@ def run_ours_single(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic" if cfg is CFG else "synthetic, drawn on the device",
         "config": {"workload": workload + ", recompute Function", **cfg, "parallelism": "tp1",
+                   "dw2_mode": mode,
                    "l2": f"working set > L2 (preact alone {M * 2 * H * 2 / 2**20:.0f} MiB)"},
         "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 6 * args.steps,
-        "frac_of_peak": {"sustained": round(value / peak, 4),
-                         "burst": round(value / float(peaks["bf16_tflops"]), 4), "source": peak_src},
-        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(ach / peak, 4),
+        "gpu_launches": launches,
+        "frac_of_peak": {"burst": round(value / burst, 4), "sustained": round(value / sustained, 4),
+                         "source": peak_src},
+        # The timed steps are a short burst (clocks in "clocks"), so the
+        # dominant kernel is held against the burst peak.
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(ach, 2), "peak": burst,
+                     "unit": "TFLOP/s", "frac": round(ach / burst, 4),
+                     "frac_of_sustained_peak": round(ach / sustained, 4),
                      "traffic": profile_traffic(dom) if cfg is CFG else None,
-                     "peak_kind": f"bf16_tflops_sustained ({peak_src})"},
+                     "peak_kind": f"bf16_tflops, burst ({peak_src})"},
         "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
-        "variants": {"dw2_prologue": {"ms_per_step": round(ms_prologue, 4),
-                                      "value": round(fl / (ms_prologue * 1e-3) / 1e12, 2),
-                                      "note": "dW2 with h recomputed in its operand prologue, "
-                                              "no [M, H] buffer in backward"}},
+        "kernels_sum_ms": round(sum(kt.values()), 4),
+        "variants": {f"dw2_{other}": {"ms_per_step": round(ms_other, 4),
+                                      "value": round(fl / (ms_other * 1e-3) / 1e12, 2)}},
         "clocks": clk.summary(),
     }
+    if not args.no_same_box and cfg is CFG:
+        line["same_box"] = same_box_comparison(args, make_step, model, params, w1, w2, dev, st, fl, ms)
     if not args.no_stack and cfg is CFG:
         peak, sms = stacked_depth(8, dev)
         line["stacked"] = {"n_blocks": 8, "peak_mib": round(peak, 1), "ms_per_step": round(sms, 3),
+                           "dw2_mode": mode,
                            "reference_recompute_peak_mib": REFERENCE_STACK_PEAK_MIB[8],
-                           "method": "max_memory_allocated - base over fwd+grad, min of 3 (as the reference)"}
-        ops.set_dw2_mode("prologue")
+                           "reference_recompute_ms_per_step": REFERENCE_STACK_MS[8],
+                           "method": "max_memory_allocated - base over fwd+grad, min of 3 (as the reference)",
+                           "not_counted": f"the stream-K workspace ({ops.STREAM_WORKSPACE_BYTES >> 20} MiB per "
+                                          "stream, allocated on the stream's first use and held for the "
+                                          "process) exists before base is taken"}
+        ops.set_dw2_mode(other)
         try:
-            peak_pro, ms_pro = stacked_depth(8, dev)
+            peak_o, ms_o = stacked_depth(8, dev)
         finally:
-            ops.set_dw2_mode("emit_h")
-        line["variants"]["dw2_prologue"]["stacked"] = {"n_blocks": 8, "peak_mib": round(peak_pro, 1),
-                                                       "ms_per_step": round(ms_pro, 3)}
+            ops.set_dw2_mode(mode)
+        line["variants"][f"dw2_{other}"]["stacked"] = {"n_blocks": 8, "peak_mib": round(peak_o, 1),
+                                                       "ms_per_step": round(ms_o, 3)}
         peak_fc, ms_fc = stacked_depth(8, dev, module="SwiGLUMLPFullCheckpoint")
         line["stacked_full_checkpoint"] = {"n_blocks": 8, "peak_mib": round(peak_fc, 1),
                                            "ms_per_step": round(ms_fc, 3)}
@@ -666,6 +749,46 @@ def run_ours_single(args):
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                                 "sample": sample}
     return line
+
+
+def same_box_comparison(args, make_step, model, params, w1, w2, dev, st, fl, ms_burst):
+    """The reference's recompute algorithm on this GPU (cuBLAS GEMMs + Inductor
+    pointwise, reference_recompute_module) against this library's step:
+    ms per step as a burst of `args.steps` steps and sustained (after
+    `args.sustained_seconds` of back-to-back steps, at the power-capped
+    clock), each with its sampled clocks."""
+    out = {"reference_algorithm": "swiglu_recompute.py:58-78 in torch ops: cuBLAS bf16 GEMMs, "
+                                  "Inductor-compiled pointwise helpers (torch.compile), same inputs",
+           "triton_fused_forwards": "not run: the reference's Triton source does not travel to the GPU box"}
+    try:
+        ref = reference_recompute_module(model.dim, model.hidden_dim, model.out_dim, w1, w2, dev)
+        ref_step = make_step(ref, list(ref.parameters()))
+        for _ in range(max(3, args.warmup)):
+            ref_step()                         # includes Inductor's compile on the first call
+        torch.cuda.synchronize()
+        time.sleep(1.0)
+        with ClockSampler(0) as c0:
+            time.sleep(0.3)
+            ref_burst = _timed_steps(ref_step, args.steps, st)
+        with ClockSampler(0) as c1:
+            ref_sus = _sustained_ms(ref_step, args.steps, st, args.sustained_seconds, ref_burst)
+        ours = make_step(model, params)
+        with ClockSampler(0) as c2:
+            ours_sus = _sustained_ms(ours, args.steps, st, args.sustained_seconds, ms_burst)
+        del ref, ref_step
+        torch.cuda.empty_cache()
+    except Exception as e:  # the comparison arm must not take the bench line down
+        out["error"] = f"{type(e).__name__}: {e}"[:300]
+        return out
+    out.update({
+        "reference_burst_ms": round(ref_burst, 4), "reference_burst_clocks": c0.summary(),
+        "reference_sustained_ms": round(ref_sus, 4), "reference_sustained_clocks": c1.summary(),
+        "ours_burst_ms": round(ms_burst, 4),
+        "ours_sustained_ms": round(ours_sus, 4), "ours_sustained_clocks": c2.summary(),
+        "speedup_burst": round(ref_burst / ms_burst, 4), "speedup_sustained": round(ref_sus / ours_sus, 4),
+        "sustained_seconds": args.sustained_seconds,
+    })
+    return out
 
 
 def run_ours_tp(args):
@@ -780,6 +903,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-stack", action="store_true", help="skip the 8-block stacked-depth memory run")
+    ap.add_argument("--no-same-box", action="store_true",
+                    help="skip the same-GPU comparison with the reference's recompute algorithm")
+    ap.add_argument("--sustained-seconds", type=float, default=3.0,
+                    help="back-to-back run before the sustained timings of the same-GPU comparison")
     ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "dw2gemm", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)

@@ -160,11 +160,12 @@ def reference_path_bf16(x, w1_rows, w2, grad_y, *, h_from_accumulator: bool = Fa
 def bf16_resolution(ref: torch.Tensor) -> float:
     """One bf16 ulp of the largest |element| of `ref`, relative to it: the
     smallest non-zero rel_max that two bf16 results can have when the
-    largest element itself differs by a rounding flip (between 2^-8 and 2^-7)."""
+    largest element itself differs by a rounding flip (between 2^-8 and 2^-7),
+    with 1e-6 of it to spare for rel_max's own f32 evaluation."""
     m = ref.double().abs().max().item()
     if m == 0.0:
         return 0.0
-    return 2.0 ** (math.floor(math.log2(m)) - 7) / m
+    return 2.0 ** (math.floor(math.log2(m)) - 7) / m * (1.0 + 1e-6)
 
 
 def bf16_ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

@@ -70,3 +70,16 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_launch_labels_of_both_dw2_modes():
+    fwd = ["swiglu_b200_fused_matmul_swiglu_save_preact", "swiglu_b200_matmul_tiled"]
+    emit = fwd + ["swiglu_b200_bwd_grad_preact_inplace_emit_h"] + ["swiglu_b200_matmul_tiled"] * 3
+    pro = fwd + ["swiglu_b200_bwd_dw2", "swiglu_b200_bwd_grad_preact_inplace"] + ["swiglu_b200_matmul_tiled"] * 2
+    assert bench.label_launches(emit * 2) == ["gemm1_swiglu", "gemm2_y", "gradh_dswiglu_emit_h", "dw2_gemm",
+                                              "dw1", "dx"] * 2
+    assert bench.label_launches(pro * 2) == ["gemm1_swiglu", "gemm2_y", "dw2_hprologue", "gradh_dswiglu",
+                                             "dw1", "dx"] * 2
+    kf = bench.kernel_flops(**bench.CFG)
+    for seq in (emit, pro):
+        assert sum(kf[k] for k in bench.label_launches(seq)) == pytest.approx(bench.flops_fwd_bwd(**bench.CFG))
