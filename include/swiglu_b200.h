@@ -222,6 +222,35 @@ int swiglu_b200_backward_logic(const void* preact, const void* grad_h, void* gra
 int swiglu_b200_pack_weight_chunked(const void* src, void* dst, int64_t K, int64_t N_half, int64_t block_n_half,
                                     int dtype, int unpack, void* stream);
 
+/* e4m3 (FP8) operand path. No counterpart in the reference, which computes
+ * in bf16/fp32 only: the same GEMMs with 8-bit operands on the tensor core's
+ * f8f6f4 kind, for the forward of a block whose inputs tolerate e4m3
+ * rounding. Operands are row-scaled: row r of an [R, C] matrix is stored as
+ * q[r, :] = e4m3(v[r, :] * 448 / amax_r) with the f32 dequantisation factor
+ * s_r = amax_r / 448 (1 for an all-zero row); products are accumulated in
+ * f32 and scaled by s_a[row] * s_b[col] in the epilogue.
+ *
+ * Quantises the bf16 matrix src [rows, cols] (cols % 8 == 0) into e4m3 bytes
+ * dst [rows, cols] and row_scale [rows]. */
+int swiglu_b200_quantize_rows_e4m3(const void* src, void* dst, float* row_scale, int64_t rows, int64_t cols,
+                                   int dtype, void* stream);
+
+/* GEMM1 + SwiGLU with e4m3 operands: preact [M, 2H] (bf16, may be NULL) and
+ * h [M, H] (bf16, may be NULL) from xq [M, K] (row scales x_scale [M]) and
+ * w1q [2H, K] (rows in `layout` order: [left | gate] or the 128-chunk
+ * interleave; row scales w1_scale [2H]). The bf16 form of the same step is
+ * swiglu_b200_fused_matmul_swiglu_save_preact (fused_forward.py:188-256,
+ * swiglu_recompute.py:61,64). K % 16 == 0, H % 32 == 0. */
+int swiglu_b200_fused_matmul_swiglu_e4m3(const void* xq, const float* x_scale, const void* w1q, const float* w1_scale,
+                                         void* preact, void* h, int64_t M, int64_t K, int64_t H, int layout,
+                                         int h_from_rounded_preact, int group_size_m, void* stream);
+
+/* C [M, N] = (A . B^T) scaled: aq [M, K] with a_scale [M], bq [N, K] with
+ * b_scale [N], both e4m3 K-major; C in out_dtype. The e4m3 form of
+ * y = h . W2^T (swiglu_recompute.py:65). K % 16 == 0, N % 8 == 0. */
+int swiglu_b200_matmul_e4m3(const void* aq, const float* a_scale, const void* bq, const float* b_scale, void* c,
+                            int64_t M, int64_t N, int64_t K, int out_dtype, int group_size_m, void* stream);
+
 /* Whole forward of one MLP block: preact (saved for backward), h (caller's
  * transient workspace [M, H]) and y [M, Dout].
  * SwiGLUMemoryOptimizedFunction.forward (swiglu_recompute.py:59-66),

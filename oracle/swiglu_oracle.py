@@ -201,3 +201,46 @@ def make_inputs(M: int, D: int, H: int, Dout: int, seed: int = 0, dtype=torch.fl
     w2 = torch.randn(Dout, H, generator=g) * H ** -0.5
     gy = torch.randn(M, Dout, generator=g)
     return tuple(t.to(dtype) for t in (x, w1, w2, gy))
+
+
+# ---------------------------------------------------------------- e4m3 path
+# The library's FP8 forward has no counterpart in the reference (which runs
+# bf16 / fp32 only). These restate the library's own definitions so its
+# kernels can be checked: per-row e4m3 quantisation, then the reference's
+# forward math (swiglu_recompute.py:61-65) on the dequantised operands.
+def quantize_rows_e4m3(t: torch.Tensor):
+    """(q float8_e4m3fn [R, C], scale f32 [R]) of a 2-D tensor: amax_r = max
+    |v| over row r, q = e4m3(v * (448 / amax_r)) rounded to nearest even
+    (|v * 448 / amax_r| <= 448, so nothing saturates beyond the largest
+    finite value), scale_r = amax_r / 448; an all-zero row gets scale 1. Both
+    divisions in f32, as the kernel does them."""
+    v = t.float()
+    amax = v.abs().amax(dim=1)
+    nz = amax > 0
+    one = torch.ones_like(amax)
+    qs = torch.where(nz, torch.full_like(amax, 448.0) / amax, one)
+    scale = torch.where(nz, amax / torch.full_like(amax, 448.0), one)
+    q = (v * qs[:, None]).to(torch.float8_e4m3fn)
+    return q, scale
+
+
+def dequantize_rows(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """f64 values of a row-scaled e4m3 matrix."""
+    return q.double() * scale.double()[:, None]
+
+
+def fp8_forward(x, w1_rows, w2, *, h_from_rounded: bool = True, layout: str = STD):
+    """The e4m3 forward of one block in f64 from bf16 inputs: x, W1 quantised
+    per row, preact = deq(x) deq(W1)^T rounded to bf16, h = left * silu(gate)
+    (from the rounded preact, or the unrounded product) rounded to bf16, h and
+    W2 quantised per row, y = deq(h) deq(W2)^T rounded to bf16. W1's rows are
+    in `layout` order. Returns dict(preact, h, y) in f64."""
+    xq, xs = quantize_rows_e4m3(x.to(torch.bfloat16))
+    wq, ws = quantize_rows_e4m3(w1_rows.to(torch.bfloat16))
+    acc = dequantize_rows(xq, xs) @ dequantize_rows(wq, ws).t()
+    preact = _bf16(acc)
+    h = forward_logic(preact if h_from_rounded else acc, layout, True)
+    hq, hs = quantize_rows_e4m3(h.to(torch.bfloat16))
+    w2q, w2s = quantize_rows_e4m3(w2.to(torch.bfloat16))
+    y = _bf16(dequantize_rows(hq, hs) @ dequantize_rows(w2q, w2s).t())
+    return {"preact": preact, "h": h, "y": y}

@@ -181,6 +181,28 @@ int make_store_map(CUtensorMap* m, void* ptr, uint64_t N, uint64_t M, uint64_t l
   return SWIGLU_OK;
 }
 
+// e4m3 operand map: row-major [rows, K] bytes, row pitch `ld` bytes; 128-byte
+// swizzled boxes of {128 elements of K, box_rows rows}.
+int make_map_e4m3(CUtensorMap* m, const void* ptr, uint64_t K, uint64_t rows, uint64_t ld, uint32_t box_rows,
+                  const char* what) {
+  EncodeTiledFn fn;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "%s: base address is not 16-byte aligned", what);
+  if (ld % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "%s: row pitch of %llu bytes is not a multiple of 16", what,
+                (unsigned long long)ld);
+  const cuuint64_t dims[2] = {K, rows};
+  const cuuint64_t strides[1] = {ld};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SWIGLU_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", what, (int)r);
+  return SWIGLU_OK;
+}
+
 // Operand maps. K-major operand stored [rows][K]; MN-major stored [K][cols].
 int map_kmajor(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows,
                const char* what) {
@@ -452,6 +474,22 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) 
   p.tiles_m = (p.M + 127) / 128;
   // The single-SM kernel has the per-lane SwiGLU epilogue only.
   return launch_tc<TcCfg<256, A_MN, B_MN, EPI == kEpiSwigluTma ? kEpiSwiglu : EPI, F32>>(p, d, st);
+}
+
+// e4m3 GEMMs: always the 2-SM kernel (the single-SM kernel has no 8-bit
+// path), 256 x 256 or 256 x 512 pair tiles by the same size rule.
+template <int EPI, bool F32>
+int run_gemm_e4m3(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) {
+  int mode = g_gemm_path.load(std::memory_order_relaxed);
+  mode = pick_gemm_mode(p.M, p.tiles_n, EPI == kEpiStore, tile_n, d.sms, mode == 1 ? 2 : mode);
+  if (mode == 1) mode = 2;
+  p.tiles_m = (p.M + 255) / 256;
+  p.group_m = p.group_m > 1 ? p.group_m / 2 : 1;
+  if (mode == 3) {
+    p.tiles_n = (p.tiles_n + 1) / 2;
+    return launch_tc2<Tc2Cfg<false, false, EPI, F32, 2, true>>(p, d, st);
+  }
+  return launch_tc2<Tc2Cfg<false, false, EPI, F32, 1, true>>(p, d, st);
 }
 
 template <bool A_MN, bool B_MN, int EPI, bool TRANSFORM>
@@ -906,6 +944,94 @@ int op_pack(const void* src, void* dst, int64_t K, int64_t Nh, int64_t B, int dt
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "pack launch");
 }
 
+// ------------------------------------------------------------ e4m3 path
+int op_quantize_e4m3(const void* src, void* dst, float* row_scale, int64_t rows, int64_t cols, int dtype,
+                     cudaStream_t st) {
+  if (int rc = check_dims("quantize_rows_e4m3", rows, cols, 0)) return rc;
+  if (dtype != SWIGLU_BF16) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "quantize_rows_e4m3 takes bf16 rows");
+  if (int rc = check_mult8("cols", cols)) return rc;
+  if (rows == 0 || cols == 0) return SWIGLU_OK;
+  if (!src || !dst || !row_scale) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(src) % 16 || reinterpret_cast<uintptr_t>(dst) % 8 ||
+      reinterpret_cast<uintptr_t>(row_scale) % 4)
+    return fail(SWIGLU_ERR_MISALIGNED, "src must be 16-byte, dst 8-byte and row_scale 4-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  long long blocks = (rows + 7) / 8;  // a warp per row, 8 warps per block
+  const long long cap = static_cast<long long>(d->sms) * 16;
+  if (blocks > cap) blocks = cap;
+  quantize_rows_e4m3_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(src), static_cast<uint8_t*>(dst), row_scale, rows, static_cast<int>(cols));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "quantize_rows_e4m3 launch");
+}
+
+int op_swiglu_fwd_e4m3(const void* xq, const float* x_scale, const void* wq, const float* w_scale, void* preact,
+                       void* h, int64_t M, int64_t K, int64_t H, int layout, int rounded, int group_m,
+                       cudaStream_t st) {
+  if (int rc = check_dims("fused_matmul_swiglu_e4m3", M, K, 2 * H)) return rc;
+  if (int rc = check_layout(layout, H)) return rc;
+  if (K <= 0 || H <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K and H must be positive");
+  if (K % 16) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K=%lld must be a multiple of 16", (long long)K);
+  if (H % 32) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "H=%lld must be a multiple of 32", (long long)H);
+  if (group_m < 1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "group_size_m must be >= 1");
+  if (M == 0) return SWIGLU_OK;
+  if (!xq || !x_scale || !wq || !w_scale || (!preact && !h))
+    return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((preact && reinterpret_cast<uintptr_t>(preact) % 16) || (h && reinterpret_cast<uintptr_t>(h) % 16))
+    return fail(SWIGLU_ERR_MISALIGNED, "preact/h must be 16-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  TcParams p{};
+  if (int rc = make_map_e4m3(&p.tmA, xq, K, M, K, 128, "x (e4m3)")) return rc;
+  if (int rc = make_map_e4m3(&p.tmB, wq, K, 2 * H, K, 128, "W1 (e4m3)")) return rc;
+  if (preact) {
+    if (int rc = make_store_map(&p.tmC, preact, 2 * H, M, 2 * H, false)) return rc;
+  }
+  if (h) {
+    if (int rc = make_store_map(&p.tmD, h, H, M, H, false)) return rc;
+  }
+  p.out0 = preact;
+  p.out1 = h;
+  p.ld0 = 2 * H;
+  p.ld1 = H;
+  p.M = (int)M, p.N = (int)H, p.K = (int)K, p.H = (int)H, p.layout = layout;
+  p.tiles_n = (int)((H + 127) / 128);
+  p.group_m = group_m;
+  p.flags = rounded ? kFlagHFromRounded : 0;
+  p.scale_a = x_scale;
+  p.scale_b = w_scale;
+  return run_gemm_e4m3<kEpiSwigluTma, false>(p, *d, st);
+}
+
+int op_matmul_e4m3(const void* aq, const float* a_scale, const void* bq, const float* b_scale, void* c, int64_t M,
+                   int64_t N, int64_t K, int out_dtype, int group_m, cudaStream_t st) {
+  if (int rc = check_dims("matmul_e4m3", M, N, K)) return rc;
+  if (int rc = check_dtype(out_dtype)) return rc;
+  if (K <= 0) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K must be positive");
+  if (K % 16) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "K=%lld must be a multiple of 16", (long long)K);
+  if (int rc = check_mult8("N", N)) return rc;
+  if (group_m < 1) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "group_size_m must be >= 1");
+  if (M == 0 || N == 0) return SWIGLU_OK;
+  if (!aq || !a_scale || !bq || !b_scale || !c) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(c) % 16) return fail(SWIGLU_ERR_MISALIGNED, "C must be 16-byte aligned");
+  DeviceInfo* d;
+  if (int rc = current_device(&d)) return rc;
+  TcParams p{};
+  if (int rc = make_map_e4m3(&p.tmA, aq, K, M, K, 128, "A (e4m3)")) return rc;
+  if (int rc = make_map_e4m3(&p.tmB, bq, K, N, K, 128, "B (e4m3)")) return rc;
+  const bool f32 = out_dtype == SWIGLU_F32;
+  if (int rc = make_store_map(&p.tmC, c, N, M, N, f32)) return rc;
+  p.out0 = c;
+  p.ld0 = N;
+  p.M = (int)M, p.N = (int)N, p.K = (int)K;
+  p.tiles_n = (int)((N + 255) / 256);
+  p.group_m = group_m;
+  p.scale_a = a_scale;
+  p.scale_b = b_scale;
+  return f32 ? run_gemm_e4m3<kEpiStore, true>(p, *d, st) : run_gemm_e4m3<kEpiStore, false>(p, *d, st);
+}
+
 // ------------------------------------------------ no-allocation variant
 // The single-rank form of the fused reduce-scatter pipeline (scatter GEMM ->
 // signal -> reduce) with its receive buffer and flags in file-scope device
@@ -1094,6 +1220,24 @@ int swiglu_b200_backward_logic(const void* preact, const void* grad_h, void* gra
 int swiglu_b200_pack_weight_chunked(const void* src, void* dst, int64_t K, int64_t N_half, int64_t block_n_half,
                                     int dtype, int unpack, void* stream) {
   return op_pack(src, dst, K, N_half, block_n_half, dtype, unpack, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_quantize_rows_e4m3(const void* src, void* dst, float* row_scale, int64_t rows, int64_t cols,
+                                   int dtype, void* stream) {
+  return op_quantize_e4m3(src, dst, row_scale, rows, cols, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_fused_matmul_swiglu_e4m3(const void* xq, const float* x_scale, const void* w1q, const float* w1_scale,
+                                         void* preact, void* h, int64_t M, int64_t K, int64_t H, int layout,
+                                         int h_from_rounded_preact, int group_size_m, void* stream) {
+  return op_swiglu_fwd_e4m3(xq, x_scale, w1q, w1_scale, preact, h, M, K, H, layout, h_from_rounded_preact,
+                            group_size_m, static_cast<cudaStream_t>(stream));
+}
+
+int swiglu_b200_matmul_e4m3(const void* aq, const float* a_scale, const void* bq, const float* b_scale, void* c,
+                            int64_t M, int64_t N, int64_t K, int out_dtype, int group_size_m, void* stream) {
+  return op_matmul_e4m3(aq, a_scale, bq, b_scale, c, M, N, K, out_dtype, group_size_m,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int swiglu_b200_mlp_forward(const void* x, const void* w1, const void* w2, void* preact, void* h_workspace,

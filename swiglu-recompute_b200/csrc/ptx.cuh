@@ -278,6 +278,18 @@ __device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_des
       : "memory");
 }
 
+// 2-SM MMA with 8-bit floating-point operands (kind::f8f6f4; the formats come
+// from the instruction descriptor), f32 accumulation. K = 32 per instruction.
+__device__ __forceinline__ void umma_f8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on the mbarrier at `bar_cluster_addr` (this CTA's or the
 // peer's) when the pair MMAs issued so far by this thread complete.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
@@ -312,6 +324,10 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_fmt, i
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0)
+// and f32 accumulation; both operands K-major.
+__host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N) { return make_idesc_f16(M, N, 0, 0, 0, 0); }
+
 // ------------------------------------------------------------- numerics
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -327,6 +343,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
+}
+
+// Two f32 values to e4m3 (round to nearest even, saturating at +-448), packed
+// with `lo` in the low byte, as they sit in memory.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // The hardware tanh approximation (tanh.approx.f32, one MUFU operation).

@@ -249,6 +249,45 @@ __global__ void pack_chunked_kernel(const T* __restrict__ src, T* __restrict__ d
   }
 }
 
+// ----------------------------------------------------- e4m3 quantisation
+// Per-row e4m3 quantisation of a bf16 [rows, cols] matrix for the FP8 GEMMs
+// (cols % 8 == 0), one warp per row: amax_r = max |v| over the row, the
+// stored dequantisation factor s_r = amax_r / 448 (1 for an all-zero row) and
+// q = e4m3(v * (448 / amax_r)) rounded to nearest even, saturating at the
+// largest finite e4m3 value 448. Both divisions are IEEE f32, so a CPU
+// restatement reproduces q and s_r bit for bit.
+__global__ void quantize_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ src, uint8_t* __restrict__ dst,
+                                          float* __restrict__ row_scale, long long rows, int cols) {
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const int vecs = cols / 8;
+  for (long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5; r < rows; r += nwarps) {
+    const uint4* row = reinterpret_cast<const uint4*>(src + r * cols);
+    float amax = 0.0f;
+    for (int v = lane; v < vecs; v += 32) {
+      const uint4 u = row[v];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float qs = amax > 0.0f ? 448.0f / amax : 1.0f;
+    if (lane == 0) row_scale[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+    uint2* out = reinterpret_cast<uint2*>(dst + r * cols);
+    for (int v = lane; v < vecs; v += 32) {
+      const uint4 u = row[v];
+      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+      const uint32_t lo = e4m3x2(a.x * qs, a.y * qs) | (e4m3x2(b.x * qs, b.y * qs) << 16);
+      const uint32_t hi = e4m3x2(c.x * qs, c.y * qs) | (e4m3x2(d.x * qs, d.y * qs) << 16);
+      out[v] = make_uint2(lo, hi);
+    }
+  }
+}
+
 // ------------------------------------------- tensor-parallel reduce-scatter
 // Owner side: wait until every source published `epoch` (bounded), then
 // out[i, j] = sum over s = 0..world-1 of recv[s, i, j] in that fixed order.

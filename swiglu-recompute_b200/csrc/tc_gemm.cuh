@@ -87,6 +87,10 @@ struct TcParams {
   // (row pitch ld0). The buffers may be other GPUs' memory (NVLink P2P).
   float* peer[8];
   int rows_per_rank, src_rank;
+  // e4m3 GEMMs (2-SM kernel): per-row dequantisation factors of A ([M]) and
+  // of B's rows ([N]; SwiGLU: indexed by the B row of each left / gate unit).
+  const float* scale_a;
+  const float* scale_b;
   // Stream-K tail (2-SM kernel only). The last `sk_tail` tiles of the tile
   // order are each computed as `sk_split` parts over equal K ranges by
   // different CTA pairs, so the last round keeps every pair busy. Each part
@@ -284,18 +288,28 @@ struct StoreStage {
   static constexpr int kWarpBytes = 2 * ((kBoxBytes + 1023) / 1024) * 1024;
 };
 
-template <int BN, bool OUT_F32>
+// SCALED (e4m3 operands): D[row, col] is scaled by scale_a[row] * scale_b[col]
+// before it is stored.
+template <int BN, bool OUT_F32, bool SCALED = false>
 __device__ __forceinline__ void epilogue_store_tma(const TcParams& p, int pn, int row0, uint32_t t_row,
                                                    uint8_t* stage) {
   using S = StoreStage<OUT_F32>;
   constexpr int kChunks16 = S::kRowBytes / 16;  // 16-byte chunks per box row
   const uint32_t lane = threadIdx.x & 31u;
   const int n0 = pn * BN;
+  float sa = 1.0f;
+  if constexpr (SCALED) sa = row0 + static_cast<int>(lane) < p.M ? p.scale_a[row0 + lane] : 0.0f;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c * 32, r);
     tmem_ld_wait();
+    if constexpr (SCALED) {
+      const int col = n0 + c * 32 + static_cast<int>(lane);
+      const float sb = col < p.N ? p.scale_b[col] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * sa * __shfl_sync(0xffffffffu, sb, i));
+    }
     uint8_t* buf = stage + (c & 1) * (S::kWarpBytes / 2);
     // The store issued from this buffer two chunks ago (possibly in the
     // previous tile) has read it once at most one store is still reading.
@@ -347,7 +361,9 @@ __device__ __forceinline__ void stage_row32_bf16(uint8_t* box, uint32_t lane, co
   }
 }
 
-template <int BN>
+// SCALED (e4m3 operands): the left and gate accumulators of row `row` and
+// unit j are scaled by scale_a[row] * scale_b[B row of left / gate j] first.
+template <int BN, bool SCALED = false>
 __device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, int row0, uint32_t t_row,
                                                     uint8_t* stage) {
   const uint32_t lane = threadIdx.x & 31u;
@@ -356,6 +372,8 @@ __device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, i
   uint8_t* lbox = stage;
   uint8_t* gbox = stage + SwigluStage::kBoxBytes;
   uint8_t* hbox = stage + 2 * SwigluStage::kBoxBytes;
+  float sa = 1.0f;
+  if constexpr (SCALED) sa = row0 + static_cast<int>(lane) < p.M ? p.scale_a[row0 + lane] : 0.0f;
 #pragma unroll 1
   for (int c = 0; c < BN / 64; ++c) {
     const int j = j0 + c * 32;
@@ -364,11 +382,21 @@ __device__ __forceinline__ void epilogue_swiglu_tma(const TcParams& p, int pn, i
     tmem_ld_32x32b_x32(t_row + c * 32, rl);
     tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, rg);
     tmem_ld_wait();
+    float sbl = 1.0f, sbg = 1.0f;
+    if constexpr (SCALED) {
+      const int jj = j + static_cast<int>(lane);
+      sbl = jj < p.H ? p.scale_b[left_col(jj, p.H, p.layout)] : 0.0f;
+      sbg = jj < p.H ? p.scale_b[gate_col(jj, p.H, p.layout)] : 0.0f;
+    }
     float lf[32], gf[32], hf[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       float l = __uint_as_float(rl[i]);
       float g = __uint_as_float(rg[i]);
+      if constexpr (SCALED) {
+        l = l * sa * __shfl_sync(0xffffffffu, sbl, i);
+        g = g * sa * __shfl_sync(0xffffffffu, sbg, i);
+      }
       lf[i] = l;
       gf[i] = g;
       if (rounded) {

@@ -37,20 +37,29 @@ namespace swiglu {
 // accumulator fills the CTA's 512 TMEM columns: per MMA FLOP a CTA then loads
 // 25 % fewer operand bytes from L2 (A is shared by both N halves), and the
 // epilogue runs between main loops while TMA keeps filling the ring.
-template <bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_, int NSUB_ = 1>
+template <bool A_MN_, bool B_MN_, int EPI_, bool OUT_F32_, int NSUB_ = 1, bool FP8_ = false>
 struct Tc2Cfg {
   static constexpr int NSUB = NSUB_;
+  // FP8_: e4m3 operands (kind::f8f6f4), both K-major, rows scaled in the
+  // epilogue by scale_a[row] * scale_b[col] (TcParams).
+  static constexpr bool FP8 = FP8_;
+  static_assert(!FP8_ || (!A_MN_ && !B_MN_), "e4m3 operands are K-major here");
+  static_assert(!FP8_ || EPI_ == kEpiStore || EPI_ == kEpiSwigluTma, "scaled epilogues: store and SwiGLU-TMA");
   static_assert(NSUB == 1 || NSUB == 2, "one or two N=256 MMAs per k-step");
   static constexpr int BM = 256;          // pair tile rows (128 per CTA)
   static constexpr int BMH = 128;         // rows per CTA
   static constexpr int BN = 256 * NSUB;   // tile columns (BN / 2 of B per CTA)
-  static constexpr int BK = 64;
+  // One 128-byte swizzle row of K per stage: 64 bf16 or 128 e4m3 elements,
+  // four MMAs of K = 16 (bf16) or K = 32 (e4m3), 32 bytes each.
+  static constexpr int ES = FP8_ ? 1 : 2;
+  static constexpr int BK = 128 / ES;
+  static constexpr int KSTEPS = 4;
   static constexpr bool A_MN = A_MN_;
   static constexpr bool B_MN = B_MN_;
   static constexpr int EPI = EPI_;
   static constexpr bool OUT_F32 = OUT_F32_;
-  static constexpr int A_BYTES = BMH * BK * 2;         // 16 KB
-  static constexpr int SUB_B_BYTES = 128 * BK * 2;     // 16 KB: this CTA's half of one N=256 MMA's B
+  static constexpr int A_BYTES = BMH * BK * ES;        // 16 KB
+  static constexpr int SUB_B_BYTES = 128 * BK * ES;    // 16 KB: this CTA's half of one N=256 MMA's B
   static constexpr int B_BYTES = NSUB * SUB_B_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // The dSwiGLU epilogue stages preact, grad and h boxes (48 KB), one ring
@@ -191,7 +200,8 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc_f16(256, 256, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
+      constexpr uint32_t idesc = Cfg::FP8 ? make_idesc_e4m3(256, 256)
+                                          : make_idesc_f16(256, 256, 1, 1, Cfg::A_MN ? 1 : 0, Cfg::B_MN ? 1 : 0);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       // The MMAs of one k-block of one 256-column accumulator half.
@@ -199,12 +209,16 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         const uint32_t sa = smem_u32(smem + st * Cfg::STAGE_BYTES);
         const uint32_t sbs = sa + Cfg::A_BYTES + sub * Cfg::SUB_B_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
+        for (int k = 0; k < Cfg::KSTEPS; ++k) {
           const uint64_t adesc = Cfg::A_MN ? make_smem_desc_sw128(sa + k * 2048, p.mn_lbo, p.mn_sbo)
                                            : make_smem_desc_sw128(sa + k * 32, 16, 1024);
           const uint64_t bdesc = Cfg::B_MN ? make_smem_desc_sw128(sbs + k * 2048, p.mn_lbo, p.mn_sbo)
                                            : make_smem_desc_sw128(sbs + k * 32, 16, 1024);
-          umma_f16_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (!first_kb || k != 0) ? 1u : 0u);
+          if constexpr (Cfg::FP8) {
+            umma_f8_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (!first_kb || k != 0) ? 1u : 0u);
+          } else {
+            umma_f16_ss_pair(d_tmem + 256 * sub, adesc, bdesc, idesc, (!first_kb || k != 0) ? 1u : 0u);
+          }
         }
       };
       auto release = [&](uint32_t st) {
@@ -303,9 +317,9 @@ __global__ void __launch_bounds__(Cfg::NUM_THREADS, 1) tc_gemm2_kernel(const __g
         const int pns = pn * Cfg::NSUB + sub;
         const uint32_t ts = t_row + 256 * sub;
         if constexpr (Cfg::EPI == kEpiStore) {
-          epilogue_store_tma<256, Cfg::OUT_F32>(p, pns, row0, ts, store_stage);
+          epilogue_store_tma<256, Cfg::OUT_F32, Cfg::FP8>(p, pns, row0, ts, store_stage);
         } else if constexpr (Cfg::EPI == kEpiSwigluTma) {
-          epilogue_swiglu_tma<256>(p, pns, row0, ts, swiglu_stage);
+          epilogue_swiglu_tma<256, Cfg::FP8>(p, pns, row0, ts, swiglu_stage);
         } else if constexpr (Cfg::EPI == kEpiDswiglu) {
           // host ensures H % 32 == 0
           epi_ok = epi_ok && epilogue_dswiglu_tma<256>(p, pns, row0, ts, dsw_stage, dsw_bar, dsw_phase, abort_flag);

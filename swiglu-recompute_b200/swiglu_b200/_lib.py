@@ -47,6 +47,9 @@ _SIGNATURES = {
     "swiglu_b200_forward_logic": [_p, _p, _i64, _i64, _i, _i, _p],
     "swiglu_b200_backward_logic": [_p, _p, _p, _i64, _i64, _i, _i, _p],
     "swiglu_b200_pack_weight_chunked": [_p, _p, _i64, _i64, _i64, _i, _i, _p],
+    "swiglu_b200_quantize_rows_e4m3": [_p, _p, _p, _i64, _i64, _i, _p],
+    "swiglu_b200_fused_matmul_swiglu_e4m3": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p],
+    "swiglu_b200_matmul_e4m3": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _p],
     "swiglu_b200_mlp_forward":
         [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p],
     "swiglu_b200_mlp_backward":

@@ -269,3 +269,52 @@ def device_status(device: torch.device | int | None = None, clear: bool = True) 
     """Pipeline-timeout bits recorded by the kernels on `device` (0 = healthy)."""
     with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
         return _lib.device_status(clear)
+
+
+# ------------------------------------------------------------ e4m3 (FP8) path
+def quantize_rows_e4m3(t: torch.Tensor):
+    """(q, scale): row-scaled e4m3 copy of a bf16 [R, C] matrix, q [R, C]
+    (torch.float8_e4m3fn) and the f32 dequantisation factor scale [R]
+    (row r holds e4m3(v * 448 / amax_r), scale_r = amax_r / 448)."""
+    dev = _check_cuda(t)
+    if t.dtype != torch.bfloat16 or t.dim() != 2:
+        raise TypeError("quantize_rows_e4m3 takes a 2-D bf16 tensor")
+    R, C = t.shape
+    q = torch.empty((R, C), device=dev, dtype=torch.float8_e4m3fn)
+    s = torch.empty((R,), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        _call(dev, "swiglu_b200_quantize_rows_e4m3", _p(t), _p(q), _p(s), R, C, BF16, _stream(dev))
+    return q, s
+
+
+def swiglu_fwd_e4m3(xq: torch.Tensor, x_scale: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor, *,
+                    layout: int, h_from_rounded: bool, want_h: bool = True, want_preact: bool = True,
+                    group_size_m: int = DEFAULT_GROUP_M):
+    """(preact [M, 2H] or None, h [M, H] or None) in bf16 from e4m3 x [M, K]
+    and W1 [2H, K] (rows in `layout` order) with their row scales."""
+    assert want_h or want_preact
+    dev = _check_cuda(xq, x_scale, wq, w_scale)
+    M, K = xq.shape
+    n2, K2 = wq.shape
+    assert K == K2 and n2 % 2 == 0 and x_scale.shape == (M,) and w_scale.shape == (n2,)
+    H = n2 // 2
+    preact = torch.empty((M, n2), device=dev, dtype=torch.bfloat16) if want_preact else None
+    h = torch.empty((M, H), device=dev, dtype=torch.bfloat16) if want_h else None
+    with torch.cuda.device(dev):
+        _call(dev, "swiglu_b200_fused_matmul_swiglu_e4m3", _p(xq), _p(x_scale), _p(wq), _p(w_scale),
+              _p(preact), _p(h), M, K, H, layout, int(bool(h_from_rounded)), int(group_size_m), _stream(dev))
+    return preact, h
+
+
+def matmul_e4m3(aq: torch.Tensor, a_scale: torch.Tensor, bq: torch.Tensor, b_scale: torch.Tensor, *,
+                out_dtype: torch.dtype = torch.bfloat16, group_size_m: int = DEFAULT_GROUP_M) -> torch.Tensor:
+    """C [M, N] = A . B^T for e4m3 A [M, K] and B [N, K] with their row scales."""
+    dev = _check_cuda(aq, a_scale, bq, b_scale)
+    M, K = aq.shape
+    N, K2 = bq.shape
+    assert K == K2 and a_scale.shape == (M,) and b_scale.shape == (N,)
+    out = torch.empty((M, N), device=dev, dtype=out_dtype)
+    with torch.cuda.device(dev):
+        _call(dev, "swiglu_b200_matmul_e4m3", _p(aq), _p(a_scale), _p(bq), _p(b_scale), _p(out), M, N, K,
+              dtype_code(out_dtype), int(group_size_m), _stream(dev))
+    return out

@@ -182,6 +182,48 @@ class SwiGLUFullCheckpointFunction(torch.autograd.Function):
         return gx, gw1, gw2
 
 
+class SwiGLUFP8ForwardFunction(torch.autograd.Function):
+    """Forward GEMMs with e4m3 (FP8) operands, backward as the recompute Function.
+
+    x, W1, h and W2 are quantised per row (e4m3, scale amax / 448); GEMM1 +
+    SwiGLU and y = h W2^T run on the tensor core's 8-bit kind with f32
+    accumulation and the row scales applied in the epilogue. preact (bf16,
+    from the dequantised accumulator) is saved as in
+    SwiGLUMemoryOptimizedFunction, whose bf16 backward (h recomputed from
+    preact) then follows unchanged. No counterpart in the reference (bf16 /
+    fp32 only); results differ from the bf16 block by e4m3 rounding of the
+    four operands.
+    """
+
+    @staticmethod
+    def forward(ctx, x, W1, W2):
+        lead = x.shape[:-1]
+        x2 = _flatten_rows(x)
+        W1c, W2c = W1.contiguous(), W2.contiguous()
+        training = any(ctx.needs_input_grad[:3])
+        xq, xs = ops.quantize_rows_e4m3(x2)
+        w1q, w1s = ops.quantize_rows_e4m3(W1c)
+        preact, h = ops.swiglu_fwd_e4m3(xq, xs, w1q, w1s, layout=LAYOUT_STD, h_from_rounded=True,
+                                        want_preact=training)
+        del xq, w1q
+        hq, hs = ops.quantize_rows_e4m3(h)
+        del h
+        w2q, w2s = ops.quantize_rows_e4m3(W2c)
+        y = ops.matmul_e4m3(hq, hs, w2q, w2s)
+        if training:
+            ctx.save_for_backward(x2, W1c, W2c, preact)
+        ctx.x_shape = x.shape
+        return y.reshape(*lead, W2.shape[0])
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        x, W1, W2, preact = ctx.saved_tensors
+        gx, gw1, gw2 = _recompute_backward(ctx, grad_y, x, W1, W2, preact, w_form=W1_ROWS, layout=LAYOUT_STD)
+        if gx is not None:
+            gx = gx.reshape(ctx.x_shape)
+        return gx, gw1, gw2
+
+
 # -----------------------------------------------------------------------------
 # nn.Module wrapper
 # -----------------------------------------------------------------------------
@@ -207,6 +249,16 @@ class SwiGLUMLPFullCheckpoint(SwiGLUMLPCustom):
 
     def forward(self, x):
         return SwiGLUFullCheckpointFunction.apply(x, self.w1, self.w2)
+
+
+class SwiGLUMLPFP8Forward(SwiGLUMLPCustom):
+    """SwiGLUMLPCustom whose forward GEMMs take e4m3 operands (bf16 weights
+    and activations quantised per row on the fly); bf16 recompute backward."""
+
+    def forward(self, x):
+        if x.dtype != torch.bfloat16:
+            raise TypeError("the e4m3 forward takes bf16 activations")
+        return SwiGLUFP8ForwardFunction.apply(x, self.w1, self.w2)
 
 
 class SwiGLUMLPGroundTruth(nn.Module):
