@@ -685,6 +685,21 @@ def run_ours_single(args):
     finally:
         ops.set_dw2_mode(mode)
 
+    # The same step with the forward GEMMs on e4m3 operands (SwiGLUMLPFP8Forward:
+    # per-row scaled x, W1, h, W2; bf16 recompute backward), and the inference
+    # forward (no gradient: no preact saved) of both.
+    fp8 = SR.SwiGLUMLPFP8Forward(D, H, Dout, dtype=torch.bfloat16).to(dev)
+    with torch.no_grad():
+        fp8.w1.copy_(model.w1)
+        fp8.w2.copy_(model.w2)
+    step8 = make_step(fp8, list(fp8.parameters()))
+    for _ in range(2):
+        step8()
+    ms_fp8 = _timed_steps(step8, args.steps, st)
+    with torch.no_grad():
+        fwd_ms = {name: _timed_steps(lambda m=m: m(xd), args.steps, st) for name, m in (("bf16", model), ("e4m3", fp8))}
+    del fp8, step8
+
     # End to end through the public API with host buffers: every step copies
     # its x and grad_y in from pinned host memory and its grad_x out, on a copy
     # stream that runs one step ahead (inputs of step i+1 and the output of
@@ -719,7 +734,12 @@ def run_ours_single(args):
         "kernels_ms": {k: round(v, 4) for k, v in kt.items()},
         "kernels_sum_ms": round(sum(kt.values()), 4),
         "variants": {f"dw2_{other}": {"ms_per_step": round(ms_other, 4),
-                                      "value": round(fl / (ms_other * 1e-3) / 1e12, 2)}},
+                                      "value": round(fl / (ms_other * 1e-3) / 1e12, 2)},
+                     "fp8_forward": {"ms_per_step": round(ms_fp8, 4),
+                                     "value": round(fl / (ms_fp8 * 1e-3) / 1e12, 2),
+                                     "inference_forward_ms": {k: round(v, 4) for k, v in fwd_ms.items()},
+                                     "note": "forward GEMMs on e4m3 operands with per-row scales, bf16 "
+                                             "recompute backward; value counts the same FLOPs as the bf16 step"}},
         "clocks": clk.summary(),
     }
     if not args.no_same_box and cfg is CFG:

@@ -181,6 +181,30 @@ int make_store_map(CUtensorMap* m, void* ptr, uint64_t N, uint64_t M, uint64_t l
   return SWIGLU_OK;
 }
 
+// 4-D bf16 map gathering several 64-column blocks of a row-major matrix in
+// one TMA operation: dims {64 columns, rows, blocks, groups} with byte
+// strides {row pitch, 128 (next 64-column block), group_stride}; 128-byte
+// swizzled boxes of {64, box_rows, 2, 2}, laid out in shared memory as
+// [group][block][row][128 B] -- the layout four {64, box_rows} 2-D boxes at
+// (c, c + 64, c + group_stride / 2, ...) give. The caller sizes `blocks` so
+// that every in-range coordinate addresses bytes inside the row.
+int make_map_gather4(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t ld_bytes, uint64_t blocks,
+                     uint64_t group_stride, uint32_t box_rows, const char* what) {
+  EncodeTiledFn fn;
+  if (int rc = get_encode_fn(&fn)) return rc;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 || ld_bytes % 16 || group_stride % 16)
+    return fail(SWIGLU_ERR_MISALIGNED, "%s: base, row pitch and group stride must be 16-byte multiples", what);
+  const cuuint64_t dims[4] = {64, rows, blocks, 2};
+  const cuuint64_t strides[3] = {ld_bytes, 128, group_stride};
+  const cuuint32_t box[4] = {64, box_rows, 2, 2};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SWIGLU_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (CUresult %d)", what, (int)r);
+  return SWIGLU_OK;
+}
+
 // e4m3 operand map: row-major [rows, K] bytes, row pitch `ld` bytes; 128-byte
 // swizzled boxes of {128 elements of K, box_rows rows}.
 int make_map_e4m3(CUtensorMap* m, const void* ptr, uint64_t K, uint64_t rows, uint64_t ld, uint32_t box_rows,
@@ -809,6 +833,26 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   if (mode >= 2) {
     p.tiles_j = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ);
     const char* what = "dW2 (CTA pair)";
+    // One TMA operation per stage for left/gate and one for grad_y where the
+    // shapes keep every gathered block inside its row: left block b (of 64
+    // units) and gate block b at +H columns (standard) or +128 (packed); the
+    // grad_y halves 256 columns apart. A tile's left block index is at most
+    // H/64 - 2 (standard) / 2H/64 - 4 (packed), its grad_y block at most
+    // Dout/64 - 6, so `blocks` below admits every coordinate used and no
+    // in-range coordinate reaches past the row.
+    if (layout == SWIGLU_LAYOUT_STD ? H % 64 == 0 : H % 128 == 0) {
+      const uint64_t blocks = layout == SWIGLU_LAYOUT_STD ? H / 64 : 2 * H / 64 - 2;
+      const uint64_t gstride = layout == SWIGLU_LAYOUT_STD ? 2 * H : 256;
+      if (int rc = make_map_gather4(&p.tm_lg4, preact, M, 4 * H, blocks, gstride, Dw2PairCfg::BK, "preact (4-D)"))
+        return rc;
+      p.gather |= 1;
+    }
+    if (Dout % 512 == 0) {
+      if (int rc = make_map_gather4(&p.tm_gy4, gy, M, 2 * Dout, Dout / 64 - 4, 512, Dw2PairCfg::BK, "grad_y (4-D)"))
+        return rc;
+      p.gather |= 2;
+    }
+    if (int rc = make_store_map(&p.tm_out, dw2, H, Dout, H, false)) return rc;
     int cap = 0;
     if (int rc = pair_capacity<dw2_hprologue_pair_kernel>(Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES, *d, &cap,
                                                          what))

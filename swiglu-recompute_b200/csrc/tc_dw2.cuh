@@ -24,6 +24,17 @@ namespace swiglu {
 struct Dw2Params {
   CUtensorMap tm_pre;  // preact [M, 2H], box {64 cols, BK tokens}
   CUtensorMap tm_gy;   // grad_y [M, Dout], box {64 outs, BK tokens}
+  // CTA-pair kernel, where the shapes allow (`gather` bits): one TMA
+  // operation per stage for all four left/gate boxes (bit 0; map {64 cols,
+  // tokens, 64-col blocks, left/gate}) and one for all four grad_y boxes
+  // (bit 1; map {64 outs, tokens, 64-col blocks, 256-col halves}), in the
+  // same shared-memory layout as the four 2-D boxes each replaces.
+  CUtensorMap tm_lg4;
+  CUtensorMap tm_gy4;
+  int gather;
+  // dW2 [Dout, H] in {32 units x 32 outputs} boxes, 64-byte swizzle: the
+  // CTA-pair kernel's epilogue stores through shared memory and TMA.
+  CUtensorMap tm_out;
   __nv_bfloat16* dw2;  // [Dout, H]
   int M, H, Dout;
   int layout;
@@ -294,7 +305,12 @@ struct Dw2PairCfg {
   static_assert(NUM_XFORM_WARPS % XFORM_GROUPS == 0, "equal prologue groups");
   static constexpr int NUM_THREADS = 32 * (2 + 4 + NUM_XFORM_WARPS);
   static constexpr int TMEM_COLS = 512;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * (4 * STAGES + 3) + 16;
+  // Epilogue staging after the ring and its barriers: per epilogue warp two
+  // {32 x 32} bf16 boxes (2 KB each) for the transposed TMA stores.
+  static constexpr int BAR_BYTES = 8 * (4 * STAGES + 3) + 16;
+  static constexpr int EPI_BOX_BYTES = 32 * 64;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES + ((BAR_BYTES + 1023) / 1024) * 1024;
+  static constexpr int SMEM_BYTES = 1024 + EPI_OFFSET + 4 * 2 * EPI_BOX_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -354,6 +370,8 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_pre);
       tma_prefetch_desc(&p.tm_gy);
+      if (p.gather & 1) tma_prefetch_desc(&p.tm_lg4);
+      if (p.gather & 2) tma_prefetch_desc(&p.tm_gy4);
       uint32_t stage = 0, phase = 0, filled = 0, fill_parity = 0;
       bool ok = true;
       for (int u = first_unit; u < num_units && ok; u += unit_step) {
@@ -374,16 +392,24 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
           uint8_t* sb = sg + C::G_BYTES;
           const int t0 = kb * BK;
           mbar_arrive_expect_tx(&lg_full[stage], C::A_BYTES + C::G_BYTES);
-          tma_load_2d(sa, &p.tm_pre, &lg_full[stage], lc, t0);
-          tma_load_2d(sa + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], lc + 64, t0);
-          tma_load_2d(sg, &p.tm_pre, &lg_full[stage], gc, t0);
-          tma_load_2d(sg + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], gc + 64, t0);
+          if (p.gather & 1) {
+            tma_load_4d(sa, &p.tm_lg4, &lg_full[stage], 0, t0, lc / 64, 0);
+          } else {
+            tma_load_2d(sa, &p.tm_pre, &lg_full[stage], lc, t0);
+            tma_load_2d(sa + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], lc + 64, t0);
+            tma_load_2d(sg, &p.tm_pre, &lg_full[stage], gc, t0);
+            tma_load_2d(sg + C::BOX_BYTES, &p.tm_pre, &lg_full[stage], gc + 64, t0);
+          }
           const uint32_t bbar = map_to_rank(&b_full[stage], 0);
           if (leader) mbar_arrive_expect_tx(&b_full[stage], 2 * C::B_BYTES);
-          tma_load_2d_pair(sb, &p.tm_gy, bbar, d0, t0);
-          tma_load_2d_pair(sb + C::BOX_BYTES, &p.tm_gy, bbar, d0 + 64, t0);
-          tma_load_2d_pair(sb + 2 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 256, t0);
-          tma_load_2d_pair(sb + 3 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 320, t0);
+          if (p.gather & 2) {
+            tma_load_4d_pair(sb, &p.tm_gy4, bbar, 0, t0, d0 / 64, 0);
+          } else {
+            tma_load_2d_pair(sb, &p.tm_gy, bbar, d0, t0);
+            tma_load_2d_pair(sb + C::BOX_BYTES, &p.tm_gy, bbar, d0 + 64, t0);
+            tma_load_2d_pair(sb + 2 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 256, t0);
+            tma_load_2d_pair(sb + 3 * C::BOX_BYTES, &p.tm_gy, bbar, d0 + 320, t0);
+          }
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -452,8 +478,7 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
       if (!mbar_wait(tmem_full, acc_phase, abort_flag, status, kErrTimeoutEpilogue)) break;
       tc_fence_after_sync();
       const int j_in_tile = C::BJH * static_cast<int>(rank) + static_cast<int>(q * 32 + lane);
-      const int j = tj * C::BJ + j_in_tile;
-      const bool j_ok = j < p.H;
+      const int jw = tj * C::BJ + C::BJH * static_cast<int>(rank) + static_cast<int>(q * 32);  // warp's first unit
       const int d0 = td * C::BD;
       const uint32_t t_row = tmem_base + ((q * 32u) << 16);
       bool finish = true;
@@ -466,18 +491,33 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
         finish = sk_publish_and_fix(t_row, C::BD, const_cast<float*>(fix) + w.part * part_stride, fix, part_stride,
                                     w.parts, p.sk_counters + i * 8 + rank * 4 + q, p.sk_epoch);
       }
+      // D is hidden-major (lane = unit) and dW2 output-major: each 32-output
+      // chunk is transposed into a {32 units x 32 outputs} box (row i =
+      // output dc + i, 64-byte rows, 64-byte swizzle: 16-byte chunk k of row
+      // i at k ^ ((i >> 1) & 3)) and leaves with one TMA store, which skips
+      // the parts of the box beyond H or Dout.
+      uint8_t* ebuf = smem + C::EPI_OFFSET + q * 2 * C::EPI_BOX_BYTES;
 #pragma unroll 1
       for (int c = 0; c < (finish ? C::BD / 32 : 0); ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         const int dc = d0 + c * 32;
-        if (j_ok) {
-          __nv_bfloat16* col = p.dw2 + static_cast<long long>(dc) * p.H + j;
+        uint8_t* buf = ebuf + (c & 1) * C::EPI_BOX_BYTES;
+        // The store issued from this buffer two chunks ago (possibly in the
+        // previous tile) has read it once at most one store is still reading.
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (dc + i < p.Dout) col[static_cast<long long>(i) * p.H] = __float2bfloat16_rn(__uint_as_float(r[i]));
-          }
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t off = i * 64 + ((((lane >> 3) ^ ((i >> 1) & 3u))) << 4) + (lane & 7u) * 2;
+          *reinterpret_cast<__nv_bfloat16*>(buf + off) = __float2bfloat16_rn(__uint_as_float(r[i]));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && jw < p.H && dc < p.Dout) {
+          tma_store_2d(&p.tm_out, buf, jw, dc);
+          bulk_commit();
         }
       }
       tc_fence_before_sync();
@@ -485,6 +525,8 @@ __global__ void __launch_bounds__(Dw2PairCfg::NUM_THREADS, 1)
       if (lane == 0) mbar_arrive_cluster(map_to_rank(tmem_empty, 0));
       acc_phase ^= 1;
     }
+    // The TMA stores read shared memory asynchronously: finish before exit.
+    if (lane == 0) bulk_wait_read<0>();
   } else {
     // The prologue warps form C::XFORM_GROUPS groups and ring slot s belongs
     // to group s % G (G divides STAGES), so G stages are transformed
