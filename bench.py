@@ -248,15 +248,16 @@ def run_kernel_only(args):
     x, w1, w2, gy = (t.to(dev) for t in _inputs(dev))
     preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
     k = args.kernel
+    gm = {} if args.group_m is None else {"group_size_m": args.group_m}
     calls = {
-        "gemm1": lambda: ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True),
-        "y": lambda: ops.matmul(h, w2, a_t=False, b_t=True),
+        "gemm1": lambda: ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True, **gm),
+        "y": lambda: ops.matmul(h, w2, a_t=False, b_t=True, **gm),
         "dw2": lambda: ops.bwd_dw2(gy, preact, layout=LAYOUT_STD),
-        "dw2gemm": lambda: ops.matmul(gy, h, a_t=True, b_t=False),
+        "dw2gemm": lambda: ops.matmul(gy, h, a_t=True, b_t=False, **gm),
         # in place on a scratch copy so repeated launches see the same input
         "gradh": lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD, h_out=h),
-        "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512),
-        "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512),
+        "dw1": lambda: ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512, **gm),
+        "dx": lambda: ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512, **gm),
     }
     pre2 = torch.empty_like(preact) if k == "gradh" else None
     fl = kernel_flops(M, D, H, Dout)[{"gemm1": "gemm1_swiglu", "y": "gemm2_y", "dw2": "dw2_hprologue",
@@ -930,6 +931,8 @@ def main():
     ap.add_argument("--kernel", choices=["gemm1", "y", "dw2", "dw2gemm", "gradh", "dw1", "dx"],
                     help="launch only this kernel (profiling case)")
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--group-m", type=int, default=None,
+                    help="with --kernel: L2 tile grouping in 128-row tiles (the reference's GROUP_SIZE_M)")
     ap.add_argument("--fwd-sweep", action="store_true",
                     help="forward-only W1 projection + SwiGLU vs cuBLAS, config 3 M sweep (not the bench line)")
     ap.add_argument("--stack-sweep", action="store_true",

@@ -10,12 +10,13 @@ What runs underneath is libswiglu_b200.so (hand-written sm_100a kernels):
   forward   one tcgen05 GEMM whose epilogue writes preact and h
             (h from the bf16-rounded preact, as swiglu_recompute.py:64 does),
             then y = h @ W2.t() on tcgen05; h is a transient buffer.
-  backward  grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
-            written over preact in place (grad_h never stored, no cat); the
-            same epilogue writes the recomputed h to a transient buffer and
-            dW2 = grad_y.t() @ h (or, in the "prologue" dW2 mode, dW2
-            recomputes h inside its operand prologue, no [M, H] buffer);
+  backward  dW2 = grad_y.t() @ h with h recomputed from preact inside the
+            dW2 kernel's operand prologue (no [M, H] buffer); then
+            grad_h = grad_y @ W2 with the SwiGLU derivative in the epilogue,
+            written over preact in place (grad_h never stored, no cat);
             dW1 = grad_preact.t() @ x and dx = grad_preact @ W1 on tcgen05.
+            (ops.set_dw2_mode("emit_h") instead has the grad_h epilogue
+            write h to a transient buffer for a plain dW2 GEMM.)
 fp32 inputs run the same dataflow on fp32 FFMA kernels (correctness mode).
 
 Shapes:  x [M, D]   W1 [2H, D]   W2 [Dout, H]
@@ -66,12 +67,12 @@ def _recompute_backward(ctx, grad_y, x, w1, w2, preact, *, w_form, layout):
     """Shared backward of the three recompute Functions.
 
     The grad_h GEMM overwrites preact with grad_preact in place; dW1 / dx
-    read grad_preact. dW2 is formed by `ops.dw2_mode()`: "emit_h" (default)
-    has the same grad_h epilogue write the recomputed h (swiglu_recompute.py:71)
-    to a transient [M, H] buffer, and dW2 = grad_y^T h is a plain GEMM;
-    "prologue" runs the dW2 kernel that recomputes h in its operand prologue
-    first, while preact is intact (no [M, H] buffer). When only dW2 is needed
-    the prologue kernel always runs. preact is internal to the Function (never
+    read grad_preact. dW2 is formed by `ops.dw2_mode()`: "prologue" (default)
+    runs the dW2 kernel that recomputes h (swiglu_recompute.py:71) in its
+    operand prologue first, while preact is intact (no [M, H] buffer);
+    "emit_h" has the grad_h epilogue write the recomputed h to a transient
+    [M, H] buffer, and dW2 = grad_y^T h is a plain GEMM. When only dW2 is
+    needed the prologue kernel always runs. preact is internal to the Function (never
     a graph output), so consuming it is safe; its version counter is bumped so
     that a second backward through the same graph raises instead of reading
     grad_preact as preact.

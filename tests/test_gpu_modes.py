@@ -5,9 +5,9 @@
 - SwiGLUFullCheckpointFunction saves only x and recomputes preact in backward;
   its outputs and gradients must equal SwiGLUMemoryOptimizedFunction's bit for
   bit, it must not save an [M, 2H] tensor, and its peak memory is lower.
-- The two dW2 modes of the backward ("emit_h": h written by the grad_h
-  epilogue, dW2 a plain GEMM; "prologue": h recomputed in the dW2 kernel's
-  operand prologue) give bit-identical y, dx and dW1 and dW2 within the bf16
+- The two dW2 modes of the backward ("prologue", the default: h recomputed
+  in the dW2 kernel's operand prologue; "emit_h": h written by the grad_h
+  epilogue, dW2 a plain GEMM) give bit-identical y, dx and dW1 and dW2 within the bf16
   bound of each other and of the oracle, for every module.
 """
 import pytest
@@ -103,6 +103,8 @@ def test_dw2_modes_agree(M, D, H, Dout):
     ref = O.mlp_forward_backward(x.float(), w1.float(), w2.float(), gy.float(), bf16=True)
     for m in _mods(D, H, Dout, w1, w2):
         res = {}
+        default = ops.dw2_mode()
+        assert default == "prologue"          # the north star's backward is the default
         for mode in ops.DW2_MODES:
             ops.set_dw2_mode(mode)
             try:
@@ -110,7 +112,7 @@ def test_dw2_modes_agree(M, D, H, Dout):
                 y = m(xd)
                 res[mode] = [y.detach()] + list(torch.autograd.grad(y, [xd] + list(m.parameters()), gy.cuda()))
             finally:
-                ops.set_dw2_mode("emit_h")
+                ops.set_dw2_mode(default)
         a, b = res["emit_h"], res["prologue"]
         name = type(m).__name__
         for i in range(3):                        # y, dx, grad of the first-layer weight

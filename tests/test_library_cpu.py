@@ -25,8 +25,9 @@ def traced(monkeypatch):
     monkeypatch.setattr(library, "kernels", lambda: library._Traced)
     for mod in (SR, FF, FP):
         monkeypatch.setattr(mod, "kernels", lambda: library._Traced)
+    default = ops.dw2_mode()
     yield
-    ops.set_dw2_mode("emit_h")
+    ops.set_dw2_mode(default)
 
 
 def _trace(fn, w1_shape):
