@@ -838,8 +838,9 @@ def run_ours_tp(args):
         x, w1, w2, gy = _inputs(dev, cfg=cfg)
         ms_rows = M // world
         fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
-        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
-                                        fused_rs=None if fused else False).to(dev).load_full(w1, w2)
+        chunks = int(os.environ.get("SWIGLU_TP_CHUNKS", "1"))
+        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16, fused_rs=None if fused else False,
+                                        chunks=chunks).to(dev).load_full(w1, w2)
         params = list(model.parameters())
         x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
         gy_l = gy[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
@@ -902,6 +903,7 @@ def run_ours_tp(args):
                        "parallelism": f"tp{world}",
                        "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
                                   if fused else "f32 partials, NCCL reduce-scatter"),
+                       "chunks": chunks, "dw2_mode": ops.dw2_mode(),
                        "l2": "working set > L2"},
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),

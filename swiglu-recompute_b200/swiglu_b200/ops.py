@@ -149,12 +149,14 @@ def _same_dtype(*ts: torch.Tensor) -> torch.dtype:
 
 def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
                h_from_rounded: bool, want_h: bool = True, want_preact: bool = True,
-               group_size_m: int = DEFAULT_GROUP_M):
+               group_size_m: int = DEFAULT_GROUP_M, preact_out: torch.Tensor | None = None,
+               h_out: torch.Tensor | None = None):
     """(preact [M, 2H] or None, h [M, H] or None) for preact = x . W1^T in one
-    launch. want_preact=False is the no-save (inference) forward."""
+    launch. want_preact=False is the no-save (inference) forward. preact_out /
+    h_out: contiguous buffers to write into instead of new ones."""
     assert want_h or want_preact
-    dev = _check_cuda(x, w)
-    dt = _same_dtype(x, w)
+    dev = _check_cuda(x, w, preact_out, h_out)
+    dt = _same_dtype(x, w, preact_out, h_out)
     M, K = x.shape
     if w_form == W1_ROWS:
         n2, K2 = w.shape
@@ -162,8 +164,13 @@ def swiglu_fwd(x: torch.Tensor, w: torch.Tensor, *, w_form: int, layout: int,
         K2, n2 = w.shape
     assert K == K2 and n2 % 2 == 0, f"shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}"
     H = n2 // 2
-    preact = torch.empty((M, n2), device=dev, dtype=dt) if want_preact else None
-    h = torch.empty((M, H), device=dev, dtype=dt) if want_h else None
+    if preact_out is not None:
+        assert want_preact and preact_out.shape == (M, n2)
+    if h_out is not None:
+        assert want_h and h_out.shape == (M, H)
+    preact = (preact_out if preact_out is not None else torch.empty((M, n2), device=dev, dtype=dt)) \
+        if want_preact else None
+    h = (h_out if h_out is not None else torch.empty((M, H), device=dev, dtype=dt)) if want_h else None
     with torch.cuda.device(dev):
         _call(dev, "swiglu_b200_fused_matmul_swiglu_save_preact", _p(x), _p(w), _p(preact), _p(h),
               M, K, H, dtype_code(dt), w_form, layout, int(bool(h_from_rounded)),

@@ -190,8 +190,10 @@ class NativeCompute:
     """Per-rank compute on libswiglu_b200.so (bf16 tcgen05 or f32 kernels)."""
 
     @staticmethod
-    def swiglu_fwd(x, w1_local):
-        return ops.swiglu_fwd(x, w1_local, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+    def swiglu_fwd(x, w1_local, out=None):
+        preact_out, h_out = out if out is not None else (None, None)
+        return ops.swiglu_fwd(x, w1_local, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True,
+                              preact_out=preact_out, h_out=h_out)
 
     @staticmethod
     def matmul(a, b, *, a_t, b_t, out_dtype=None, tile_n=0):
@@ -206,20 +208,63 @@ class NativeCompute:
         return ops.bwd_grad_preact_inplace(gy, w2_local, preact, layout=LAYOUT_STD, h_out=h_out)
 
 
+def _all_gather_chunks(t_local, group, chunks):
+    """All-gather the row shard t_local [m, ...] as `chunks` row pieces, each an
+    asynchronous NCCL all-gather into its slice of one buffer: rows
+    [c*t*mc, (c+1)*t*mc) hold every rank's piece c (mc = m / chunks), rank by
+    rank. Returns (buffer, works); work c must be waited on (which orders the
+    current stream after it) before slice c is read."""
+    world = dist.get_world_size(group)
+    m = t_local.shape[0]
+    mc = m // chunks
+    out = torch.empty((m * world, *t_local.shape[1:]), dtype=t_local.dtype, device=t_local.device)
+    works = []
+    for c in range(chunks):
+        piece = t_local[c * mc:(c + 1) * mc].contiguous()
+        works.append(dist.all_gather_into_tensor(out[c * world * mc:(c + 1) * world * mc], piece, group=group,
+                                                 async_op=True))
+    return out, works
+
+
 class _TPSwiGLUFunction(torch.autograd.Function):
+    """The tensor-parallel block. With `chunks` = C > 1 each rank's token
+    shard travels as C row pieces: the all-gathers of x and grad_y are issued
+    for all pieces at once, and the GEMMs of piece c start as soon as piece c
+    has arrived while the later pieces are still in flight; y and grad_x are
+    reduce-scattered piece by piece (the reduce-scatter of piece c overlaps
+    the GEMMs of piece c + 1). Gathered rows are stored piece-major, which
+    every GEMM of the block is indifferent to (dW1 and dW2 sum over all rows
+    of both of their operands in the same order)."""
+
     @staticmethod
-    def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs):
-        x = all_gather_rows(x_local, group)
-        preact, h = compute.swiglu_fwd(x, w1_local)
-        if fused_rs is not None and fused_rs.wants(h.shape[1]):
-            y_local = fused_rs.matmul("y", h, w2_local, a_t=False, b_t=True, out_dtype=x.dtype)
-        else:
-            acc_dt = torch.float32 if reduce_f32 else x.dtype
-            y_part = compute.matmul(h, w2_local, a_t=False, b_t=True, out_dtype=acc_dt)
-            y_local = reduce_scatter_rows(y_part, group).to(x.dtype)
+    def forward(ctx, x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs, chunks=1):
+        world = dist.get_world_size(group)
+        if chunks < 1 or x_local.shape[0] % chunks:
+            chunks = 1
+        x, works = _all_gather_chunks(x_local, group, chunks)
+        rows = x.shape[0] // chunks
+        n2 = w1_local.shape[0]
+        preact = x.new_empty((x.shape[0], n2))
+        h = x.new_empty((x.shape[0], n2 // 2))
+        fused = fused_rs is not None and fused_rs.wants(h.shape[1])
+        acc_dt = torch.float32 if reduce_f32 else x.dtype
+        pending = []
+        for c in range(chunks):
+            works[c].wait()
+            sl = slice(c * rows, (c + 1) * rows)
+            compute.swiglu_fwd(x[sl], w1_local, out=(preact[sl], h[sl]))
+            if fused:
+                pending.append(fused_rs.matmul_start(("y", c), h[sl], w2_local, a_t=False, b_t=True,
+                                                     out_dtype=x.dtype))
+            else:
+                y_part = compute.matmul(h[sl], w2_local, a_t=False, b_t=True, out_dtype=acc_dt)
+                pending.append(_PendingReduceScatter(y_part, group))
         del h
+        pieces = [fused_rs.finish(p) if fused else p.wait().to(x.dtype) for p in pending]
+        y_local = pieces[0] if chunks == 1 else torch.cat(pieces)
         ctx.save_for_backward(x, w1_local, w2_local, preact)
         ctx.group, ctx.compute, ctx.reduce_f32, ctx.fused_rs = group, compute, reduce_f32, fused_rs
+        ctx.chunks, ctx.world = chunks, world
         return y_local
 
     @staticmethod
@@ -228,48 +273,57 @@ class _TPSwiGLUFunction(torch.autograd.Function):
             raise RuntimeError("tensor-parallel SwiGLU backward already consumed its saved preact")
         ctx._consumed = True
         x, w1_local, w2_local, preact = ctx.saved_tensors
-        compute = ctx.compute
-        gy = all_gather_rows(grad_y_local.to(x.dtype), ctx.group)
-        # grad_preact in place of preact; dW2 as in the single-GPU backward
-        # (ops.dw2_mode): from the h the same epilogue writes, or with h
-        # recomputed in the dW2 kernel's prologue before preact is replaced.
-        h = None
-        if ops.dw2_mode() == "emit_h":
-            h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device, dtype=preact.dtype)
-            gp = compute.grad_preact_inplace(gy, w2_local, preact, h_out=h)
-        else:
+        compute, chunks = ctx.compute, ctx.chunks
+        gy, works = _all_gather_chunks(grad_y_local.to(x.dtype).contiguous(), ctx.group, chunks)
+        rows = gy.shape[0] // chunks
+        emit = ops.dw2_mode() == "emit_h"
+        # dW2 as in the single-GPU backward (ops.dw2_mode): in the prologue
+        # mode the dW2 kernel reads every row of preact (and so of grad_y)
+        # before grad_h replaces any of it; with emit_h the grad_h epilogue
+        # writes h piece by piece and dW2 runs after the last piece.
+        if not emit:
+            for w in works:
+                w.wait()
             dw2 = compute.dw2(gy, preact)
-            gp = compute.grad_preact_inplace(gy, w2_local, preact)
+        h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device,
+                        dtype=preact.dtype) if emit else None
+        fused = ctx.fused_rs is not None and ctx.fused_rs.wants(preact.shape[1])
+        acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
+        pending = []
+        for c in range(chunks):
+            works[c].wait()
+            sl = slice(c * rows, (c + 1) * rows)
+            gp = compute.grad_preact_inplace(gy[sl], w2_local, preact[sl], h_out=h[sl] if emit else None)
+            # dx of this piece first: its reduce-scatter proceeds while the
+            # later pieces, dW2 and dW1 (no communication) compute.
+            if fused:
+                pending.append(ctx.fused_rs.matmul_start(("dx", c), gp, w1_local, a_t=False, b_t=False,
+                                                         out_dtype=x.dtype))
+            else:
+                pending.append(_PendingReduceScatter(
+                    compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt), ctx.group))
         torch.autograd.graph.increment_version(preact)
-        # dx first: its reduce-scatter (the other ranks' pushes and the owner
-        # sum, or NCCL on its own stream) proceeds while dW2 and dW1, which
-        # need no communication, compute.
-        fused = ctx.fused_rs is not None and ctx.fused_rs.wants(gp.shape[1])
-        if fused:
-            pending = ctx.fused_rs.matmul_start("dx", gp, w1_local, a_t=False, b_t=False, out_dtype=x.dtype)
-        else:
-            acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
-            pending = _PendingReduceScatter(compute.matmul(gp, w1_local, a_t=False, b_t=False, out_dtype=acc_dt),
-                                            ctx.group)
-        if h is not None:
+        gp = preact                                                  # now holds grad_preact
+        if emit:
             dw2 = compute.matmul(gy, h, a_t=True, b_t=False)
             del h
         # Tile widths of the local GEMMs by size (256 x 512 from 8 waves of
         # them): the per-rank dW1 of a sharded block is 1/t of the
         # single-GPU one, often below the size where the wide tiles win.
         dw1 = compute.matmul(gp, x, a_t=True, b_t=False)
-        if fused:
-            dx_local = ctx.fused_rs.finish(pending)
-        else:
-            dx_local = pending.wait().to(x.dtype)
-        return dx_local, dw1, dw2, None, None, None, None
+        pieces = [ctx.fused_rs.finish(p) if fused else p.wait().to(x.dtype) for p in pending]
+        dx_local = pieces[0] if chunks == 1 else torch.cat(pieces)
+        return dx_local, dw1, dw2, None, None, None, None, None
 
 
-def tp_swiglu(x_local, w1_local, w2_local, group=None, compute=NativeCompute, reduce_f32=True, fused_rs=None):
+def tp_swiglu(x_local, w1_local, w2_local, group=None, compute=NativeCompute, reduce_f32=True, fused_rs=None,
+              chunks=1):
     """y_r [M/t, Dout] for the token shard x_r [M/t, D]; see the module docstring.
     With `fused_rs` (a FusedReduceScatter) the reduce-scatters of y and grad_x
-    run inside their GEMMs over NVLink instead of as NCCL collectives."""
-    return _TPSwiGLUFunction.apply(x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs)
+    run inside their GEMMs over NVLink instead of as NCCL collectives; with
+    `chunks` > 1 the shard's collectives travel in that many row pieces,
+    overlapped with the GEMMs of the pieces already there."""
+    return _TPSwiGLUFunction.apply(x_local, w1_local, w2_local, group, compute, reduce_f32, fused_rs, chunks)
 
 
 class SwiGLUMLPTensorParallel(nn.Module):
@@ -277,9 +331,11 @@ class SwiGLUMLPTensorParallel(nn.Module):
     rank's shards: w1 [2H/t, D], w2 [Dout, H/t])."""
 
     def __init__(self, dim, hidden_dim, out_dim=None, dtype=torch.float32, group=None,
-                 reduce_f32=True, fused_rs=None):
+                 reduce_f32=True, fused_rs=None, chunks=1):
         super().__init__()
         self.group = group
+        # Row pieces the token shard's collectives travel in (tp_swiglu).
+        self.chunks = chunks
         # Fused GEMM + reduce-scatter over NVLink (bf16 only); default on for
         # bf16 when CUDA peer memory is available.
         self.fused_rs = fused_rs
@@ -305,4 +361,5 @@ class SwiGLUMLPTensorParallel(nn.Module):
             if self.fused_rs is None or self.fused_rs is True:
                 self.fused_rs = FusedReduceScatter(self.group)
             frs = self.fused_rs
-        return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32, frs)
+        return tp_swiglu(x_local, self.w1, self.w2, self.group, NativeCompute, self.reduce_f32, frs,
+                         self.chunks)

@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shape, fused, q):
+def _worker(rank, world, port, shape, fused, chunks, q):
     from datetime import timedelta
 
     import torch.distributed as dist
@@ -42,8 +42,8 @@ def _worker(rank, world, port, shape, fused, q):
         if fused:
             frs = tp.FusedReduceScatter()
             frs.K_PER_LINK_BYTE = 0          # always fuse at this small test shape
-        mlp = tp.SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16,
-                                         fused_rs=frs if fused else False).to(dev).load_full(w1, w2)
+        mlp = tp.SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16, fused_rs=frs if fused else False,
+                                         chunks=chunks).to(dev).load_full(w1, w2)
         xl = x[rank * ms:(rank + 1) * ms].to(dev).requires_grad_(True)
         y = mlp(xl)
         dx, dw1, dw2 = torch.autograd.grad(y, [xl, mlp.w1, mlp.w2], gy[rank * ms:(rank + 1) * ms].to(dev))
@@ -63,9 +63,10 @@ def _worker(rank, world, port, shape, fused, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("chunks", [1, 2], ids=["whole", "2_pieces"])
 @pytest.mark.parametrize("fused", [True, False], ids=["fused_rs", "nccl_rs"])
 @pytest.mark.parametrize("world", [2])
-def test_tensor_parallel_matches_oracle(world, fused):
+def test_tensor_parallel_matches_oracle(world, fused, chunks):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from swiglu_b200 import tp
@@ -74,7 +75,7 @@ def test_tensor_parallel_matches_oracle(world, fused):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fused, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shape, fused, chunks, q)) for r in range(world)]
     for p in procs:
         p.start()
     ys, dxs, dw1s, dw2s = q.get(timeout=300)

@@ -17,9 +17,14 @@ class OracleCompute:
     """Per-rank compute with the oracle's f32 math (test stand-in for NativeCompute)."""
 
     @staticmethod
-    def swiglu_fwd(x, w1_local):
+    def swiglu_fwd(x, w1_local, out=None):
         preact = x @ w1_local.t()
-        return preact, O.forward_logic(preact)
+        h = O.forward_logic(preact)
+        if out is not None:
+            out[0].copy_(preact)
+            out[1].copy_(h)
+            return out
+        return preact, h
 
     @staticmethod
     def matmul(a, b, *, a_t, b_t, out_dtype=None, tile_n=0):
@@ -44,7 +49,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, D, H, Dout, q, dw2_mode="emit_h"):
+def _worker(rank, world, port, M, D, H, Dout, q, dw2_mode="emit_h", chunks=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -56,7 +61,7 @@ def _worker(rank, world, port, M, D, H, Dout, q, dw2_mode="emit_h"):
         w1_l = tp.shard_w1_rows(w1, rank, world).requires_grad_(True)
         w2_l = tp.shard_w2(w2, rank, world).requires_grad_(True)
         x_l = x[rank * ms:(rank + 1) * ms].clone().requires_grad_(True)
-        y_l = tp.tp_swiglu(x_l, w1_l, w2_l, None, OracleCompute, True)
+        y_l = tp.tp_swiglu(x_l, w1_l, w2_l, None, OracleCompute, True, None, chunks)
         dx_l, dw1_l, dw2_l = torch.autograd.grad(y_l, [x_l, w1_l, w2_l], gy[rank * ms:(rank + 1) * ms])
         q.put((rank, y_l.detach(), dx_l, dw1_l, dw2_l))
     finally:
@@ -65,12 +70,15 @@ def _worker(rank, world, port, M, D, H, Dout, q, dw2_mode="emit_h"):
 
 @pytest.mark.parametrize("world", [2])
 @pytest.mark.parametrize("dw2_mode", ["emit_h", "prologue"])
-def test_tp_matches_single_rank_oracle(world, dw2_mode):
+@pytest.mark.parametrize("chunks", [1, 2, 4])
+def test_tp_matches_single_rank_oracle(world, dw2_mode, chunks):
+    """The block split over two gloo ranks, its collectives in `chunks` row
+    pieces (piece-major gathered rows), against the unsplit oracle."""
     M, D, H, Dout = 64, 48, 128, 40
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, H, Dout, q, dw2_mode))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, H, Dout, q, dw2_mode, chunks))
              for r in range(world)]
     for p in procs:
         p.start()
