@@ -839,6 +839,10 @@ def run_ours_tp(args):
         ms_rows = M // world
         fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
         chunks = int(os.environ.get("SWIGLU_TP_CHUNKS", "1"))
+        sm_reserve = int(os.environ.get("SWIGLU_SM_RESERVE", "0"))
+        if sm_reserve:
+            from swiglu_b200 import _lib
+            _lib.set_sm_reserve(sm_reserve)
         model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16, fused_rs=None if fused else False,
                                         chunks=chunks).to(dev).load_full(w1, w2)
         params = list(model.parameters())
@@ -903,7 +907,7 @@ def run_ours_tp(args):
                        "parallelism": f"tp{world}",
                        "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
                                   if fused else "f32 partials, NCCL reduce-scatter"),
-                       "chunks": chunks, "dw2_mode": ops.dw2_mode(),
+                       "chunks": chunks, "sm_reserve": sm_reserve, "dw2_mode": ops.dw2_mode(),
                        "l2": "working set > L2"},
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),

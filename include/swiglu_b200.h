@@ -76,6 +76,14 @@ int swiglu_b200_device_status(uint32_t* bits, int clear);
  * their tiling at compile time, fused_forward.py:55-65). */
 int swiglu_b200_set_gemm_path(int mode);
 
+/* Number of SMs (0..64, default 0) that the persistent GEMM launches leave
+ * free from now on (process-wide): a launch then holds at most
+ * (SMs - sms) / 2 CTA pairs (or SMs - sms single CTAs), so kernels on other
+ * streams -- a collective overlapped with the GEMMs, for instance -- are not
+ * kept waiting for the GEMM's last CTA. Results are unchanged. No reference
+ * counterpart (single-GPU, one stream). */
+int swiglu_b200_set_sm_reserve(int sms);
+
 /* The kernel family swiglu_b200_matmul_tiled would run a bf16 GEMM with an
  * [M, N] output on, for a device with `num_sms` SMs: *family = 1 (single-SM),
  * 2 (CTA pair, 256 x 256 tiles) or 3 (CTA pair, 256 x 512 tiles), honouring a

@@ -244,6 +244,11 @@ constexpr uint32_t kMnSbo = 8 * 128;      // eight 128-byte swizzle rows
 // 256 x 256 tiles, 3 = 2-SM kernel with 256 x 512 tiles.
 std::atomic<int> g_gemm_path{0};
 
+// SMs the persistent launches leave free (swiglu_b200_set_sm_reserve), so
+// that kernels of other streams, e.g. NCCL collectives overlapped with the
+// GEMMs, find SMs to run on.
+std::atomic<int> g_sm_reserve{0};
+
 // Per-kernel launch state: dynamic shared memory opt-in done (bit per device)
 // and, for cluster kernels, how many CTA pairs fit at once on each device.
 struct KernelState {
@@ -269,7 +274,9 @@ int launch_single(const Params& p, int tiles, int threads, int smem, const Devic
     if (e != cudaSuccess) return cuda_fail(e, what);
     ks.ready.fetch_or(1ull << dev);
   }
-  const int grid = tiles < d.sms ? tiles : d.sms;
+  int sms = d.sms - g_sm_reserve.load(std::memory_order_relaxed);
+  if (sms < 1) sms = 1;
+  const int grid = tiles < sms ? tiles : sms;
   kern<<<grid, threads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, what);
@@ -309,7 +316,8 @@ int pair_capacity(int threads, int smem, const DeviceInfo& d, int* out, const ch
     ks.max_clusters[dev] = n;
     ks.ready.fetch_or(1ull << dev);
   }
-  *out = ks.max_clusters[dev];
+  const int keep = ks.max_clusters[dev] - (g_sm_reserve.load(std::memory_order_relaxed) + 1) / 2;
+  *out = keep < 1 ? 1 : keep;
   return SWIGLU_OK;
 }
 
@@ -1207,6 +1215,12 @@ int swiglu_b200_gemm_plan(int64_t M, int64_t N, int tile_n, int num_sms, int* fa
   if (int rc = check_dims("gemm_plan", M, N, 1)) return rc;
   if (num_sms < 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "num_sms must be >= 2");
   *family = pick_gemm_mode(M, (N + 255) / 256, true, tile_n, num_sms, g_gemm_path.load(std::memory_order_relaxed));
+  return SWIGLU_OK;
+}
+
+int swiglu_b200_set_sm_reserve(int sms) {
+  if (sms < 0 || sms > 64) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "SM reserve must be in [0, 64]");
+  g_sm_reserve.store(sms);
   return SWIGLU_OK;
 }
 

@@ -30,6 +30,7 @@ _SIGNATURES = {
     "swiglu_b200_last_error_message": [],
     "swiglu_b200_device_status": [ctypes.POINTER(ctypes.c_uint32), _i],
     "swiglu_b200_set_gemm_path": [_i],
+    "swiglu_b200_set_sm_reserve": [_i],
     "swiglu_b200_gemm_plan": [_i64, _i64, _i, _i, ctypes.POINTER(_i)],
     "swiglu_b200_set_stream_workspace": [_p, ctypes.c_size_t, _p],
     "swiglu_b200_fused_matmul_swiglu_save_preact":
@@ -115,6 +116,12 @@ def set_gemm_path(mode: int) -> None:
     """0 = by size, 1 = single-SM tcgen05 kernel, 2 = 2-SM (CTA pair) kernel with 256 x 256
     tiles, 3 = 2-SM kernel with 256 x 512 tiles."""
     call("swiglu_b200_set_gemm_path", int(mode))
+
+
+def set_sm_reserve(sms: int) -> None:
+    """SMs the persistent GEMM launches leave free for other streams' kernels
+    (process-wide; 0 = use every SM)."""
+    call("swiglu_b200_set_sm_reserve", int(sms))
 
 
 def gemm_plan(M: int, N: int, tile_n: int = 0, num_sms: int = 148) -> int:

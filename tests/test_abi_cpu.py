@@ -218,3 +218,11 @@ def test_binding_signatures_match_the_header_prototypes():
                 assert at is _SCALARS[ctype.replace("const", "").strip()], (name, decl)
         want_ret = ctypes.c_char_p if "char" in ret else ctypes.c_int
         assert _lib._RESTYPES.get(name, ctypes.c_int) is want_ret, name
+
+
+def test_sm_reserve_range(lib):
+    assert lib.swiglu_b200_set_sm_reserve(-1) == 1
+    assert lib.swiglu_b200_set_sm_reserve(65) == 1
+    assert b"SM reserve" in lib.swiglu_b200_last_error_message()
+    assert lib.swiglu_b200_set_sm_reserve(8) == 0
+    assert lib.swiglu_b200_set_sm_reserve(0) == 0
