@@ -105,6 +105,53 @@ def _(grad_y, w2, preact, layout, h_out):
     return None
 
 
+@torch.library.custom_op(f"{_NS}::quantize_e4m3", mutates_args=(), device_types="cuda")
+def quantize_e4m3(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(q e4m3 [R, C], row scales [R]) of a bf16 [R, C] matrix."""
+    return ops.quantize_rows_e4m3(t)
+
+
+@quantize_e4m3.register_fake
+def _(t):
+    return t.new_empty(t.shape, dtype=torch.float8_e4m3fn), t.new_empty((t.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op(f"{_NS}::swiglu_fwd_e4m3", mutates_args=(), device_types="cuda")
+def swiglu_fwd_e4m3(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                    layout: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(preact [M, 2H], h [M, H]) in bf16 from e4m3 x and W1 rows."""
+    return ops.swiglu_fwd_e4m3(xq, xs, wq, ws, layout=layout, h_from_rounded=True)
+
+
+@swiglu_fwd_e4m3.register_fake
+def _(xq, xs, wq, ws, layout):
+    m, n2 = xq.shape[0], wq.shape[0]
+    return (xq.new_empty((m, n2), dtype=torch.bfloat16), xq.new_empty((m, n2 // 2), dtype=torch.bfloat16))
+
+
+@torch.library.custom_op(f"{_NS}::swiglu_fwd_e4m3_h", mutates_args=(), device_types="cuda")
+def swiglu_fwd_e4m3_h(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                      layout: int) -> torch.Tensor:
+    """h [M, H] only (the no-save e4m3 forward)."""
+    return ops.swiglu_fwd_e4m3(xq, xs, wq, ws, layout=layout, h_from_rounded=True, want_preact=False)[1]
+
+
+@swiglu_fwd_e4m3_h.register_fake
+def _(xq, xs, wq, ws, layout):
+    return xq.new_empty((xq.shape[0], wq.shape[0] // 2), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op(f"{_NS}::matmul_e4m3", mutates_args=(), device_types="cuda")
+def matmul_e4m3(aq: torch.Tensor, a_scale: torch.Tensor, bq: torch.Tensor, b_scale: torch.Tensor) -> torch.Tensor:
+    """A . B^T in bf16 for e4m3 A [M, K], B [N, K] with their row scales."""
+    return ops.matmul_e4m3(aq, a_scale, bq, b_scale)
+
+
+@matmul_e4m3.register_fake
+def _(aq, a_scale, bq, b_scale):
+    return aq.new_empty((aq.shape[0], bq.shape[0]), dtype=torch.bfloat16)
+
+
 class _Eager:
     """The calls the Functions make, on the plain ops functions."""
 
@@ -135,6 +182,22 @@ class _Eager:
     def bwd_grad_preact_(grad_y, w2, preact, layout, h_out=None):
         ops.bwd_grad_preact_inplace(grad_y, w2, preact, layout=layout, h_out=h_out)
 
+    @staticmethod
+    def quantize_e4m3(t):
+        return ops.quantize_rows_e4m3(t)
+
+    @staticmethod
+    def swiglu_fwd_e4m3(xq, xs, wq, ws, layout):
+        return ops.swiglu_fwd_e4m3(xq, xs, wq, ws, layout=layout, h_from_rounded=True)
+
+    @staticmethod
+    def swiglu_fwd_e4m3_h(xq, xs, wq, ws, layout):
+        return ops.swiglu_fwd_e4m3(xq, xs, wq, ws, layout=layout, h_from_rounded=True, want_preact=False)[1]
+
+    @staticmethod
+    def matmul_e4m3(aq, a_scale, bq, b_scale):
+        return ops.matmul_e4m3(aq, a_scale, bq, b_scale)
+
 
 class _Traced:
     """The same calls as registered ops (what Dynamo records)."""
@@ -162,6 +225,22 @@ class _Traced:
     @staticmethod
     def bwd_grad_preact_(grad_y, w2, preact, layout, h_out=None):
         torch.ops.swiglu_b200.bwd_grad_preact_(grad_y, w2, preact, layout, h_out)
+
+    @staticmethod
+    def quantize_e4m3(t):
+        return torch.ops.swiglu_b200.quantize_e4m3(t)
+
+    @staticmethod
+    def swiglu_fwd_e4m3(xq, xs, wq, ws, layout):
+        return torch.ops.swiglu_b200.swiglu_fwd_e4m3(xq, xs, wq, ws, layout)
+
+    @staticmethod
+    def swiglu_fwd_e4m3_h(xq, xs, wq, ws, layout):
+        return torch.ops.swiglu_b200.swiglu_fwd_e4m3_h(xq, xs, wq, ws, layout)
+
+    @staticmethod
+    def matmul_e4m3(aq, a_scale, bq, b_scale):
+        return torch.ops.swiglu_b200.matmul_e4m3(aq, a_scale, bq, b_scale)
 
 
 def kernels():

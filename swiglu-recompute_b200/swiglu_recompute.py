@@ -202,15 +202,18 @@ class SwiGLUFP8ForwardFunction(torch.autograd.Function):
         x2 = _flatten_rows(x)
         W1c, W2c = W1.contiguous(), W2.contiguous()
         training = any(ctx.needs_input_grad[:3])
-        xq, xs = ops.quantize_rows_e4m3(x2)
-        w1q, w1s = ops.quantize_rows_e4m3(W1c)
-        preact, h = ops.swiglu_fwd_e4m3(xq, xs, w1q, w1s, layout=LAYOUT_STD, h_from_rounded=True,
-                                        want_preact=training)
+        K = kernels()
+        xq, xs = K.quantize_e4m3(x2)
+        w1q, w1s = K.quantize_e4m3(W1c)
+        if training:
+            preact, h = K.swiglu_fwd_e4m3(xq, xs, w1q, w1s, LAYOUT_STD)
+        else:
+            h = K.swiglu_fwd_e4m3_h(xq, xs, w1q, w1s, LAYOUT_STD)
         del xq, w1q
-        hq, hs = ops.quantize_rows_e4m3(h)
+        hq, hs = K.quantize_e4m3(h)
         del h
-        w2q, w2s = ops.quantize_rows_e4m3(W2c)
-        y = ops.matmul_e4m3(hq, hs, w2q, w2s)
+        w2q, w2s = K.quantize_e4m3(W2c)
+        y = K.matmul_e4m3(hq, hs, w2q, w2s)
         if training:
             ctx.save_for_backward(x2, W1c, W2c, preact)
         ctx.x_shape = x.shape

@@ -29,7 +29,7 @@ def _fwd_bwd(m, x, gy):
 
 
 @pytest.mark.parametrize("cls", [SR.SwiGLUMLPCustom, SR.SwiGLUMLPFullCheckpoint, FF.SwiGLUMLPFused,
-                                 FP.SwiGLUMLPPackedFused])
+                                 FP.SwiGLUMLPPackedFused, SR.SwiGLUMLPFP8Forward])
 def test_compiled_module_matches_eager(cls):
     torch._dynamo.reset()
     torch.manual_seed(0)

@@ -95,11 +95,28 @@ def test_inference_traces_h_only(traced):
     assert "swiglu_b200.swiglu_fwd_h.default" in t and "swiglu_b200.swiglu_fwd.default" not in t
 
 
+@pytest.mark.parametrize("mode", ["emit_h", "prologue"])
+def test_e4m3_forward_traces_through_registered_ops(traced, mode):
+    """SwiGLUFP8ForwardFunction under tracing: four quantisations, the e4m3
+    GEMM1 + SwiGLU and y GEMM, then the bf16 recompute backward, all as this
+    library's registered ops."""
+    ops.set_dw2_mode(mode)
+    g = _trace(SR.SwiGLUFP8ForwardFunction.apply, (2 * H, D))
+    t = _targets(g)
+    ours = [x for x in t if x.startswith("swiglu_b200.")]
+    assert sum(x == "swiglu_b200.quantize_e4m3.default" for x in ours) == 4
+    assert "swiglu_b200.swiglu_fwd_e4m3.default" in ours and "swiglu_b200.matmul_e4m3.default" in ours
+    assert "swiglu_b200.bwd_grad_preact_.default" in ours
+    outs = [n for n in g.graph.nodes if n.op == "output"][0].args[0]
+    assert [tuple(o.meta["val"].shape) for o in outs] == [(M, Dout), (M, D), (2 * H, D), (Dout, H)]
+
+
 def test_mutation_is_declared():
     schema = torch.ops.swiglu_b200.bwd_grad_preact_.default._schema
     written = [a.name for a in schema.arguments if a.alias_info is not None and a.alias_info.is_write]
     assert written == ["preact", "h_out"]
-    for name in ("swiglu_fwd", "swiglu_fwd_h", "swiglu_fwd_preact", "matmul", "bwd_dw2"):
+    for name in ("swiglu_fwd", "swiglu_fwd_h", "swiglu_fwd_preact", "matmul", "bwd_dw2", "quantize_e4m3",
+                 "swiglu_fwd_e4m3", "swiglu_fwd_e4m3_h", "matmul_e4m3"):
         s = getattr(torch.ops.swiglu_b200, name).default._schema
         assert not any(a.alias_info is not None and a.alias_info.is_write for a in s.arguments), name
 
