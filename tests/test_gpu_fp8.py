@@ -43,7 +43,7 @@ def test_quantize_rows_bit_exact():
 
 @pytest.mark.parametrize("layout", [O.STD, O.PACKED])
 @pytest.mark.parametrize("rounded", [True, False])
-@pytest.mark.parametrize("M,K,H", [(512, 1024, 512), (300, 256, 384), (4096, 512, 256)])
+@pytest.mark.parametrize("M,K,H", [(512, 1024, 512), (300, 256, 384), (4096, 512, 256), (256, 208, 256)])
 def test_e4m3_swiglu_forward(layout, rounded, M, K, H):
     lay = ops.LAYOUT_STD if layout == O.STD else ops.LAYOUT_PACKED128
     x = _r(M, K, seed=2)
@@ -64,7 +64,7 @@ def test_e4m3_swiglu_forward(layout, rounded, M, K, H):
 
 
 @pytest.mark.parametrize("out_dtype,tol", [(torch.bfloat16, BF16_TOL), (torch.float32, 1e-4)])
-@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (333, 264, 128), (4096, 1024, 3584)])
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (333, 264, 128), (4096, 1024, 3584), (256, 256, 144)])
 def test_e4m3_matmul(out_dtype, tol, M, N, K):
     a = _r(M, K, seed=4)
     b = _r(N, K, seed=5, scale=K ** -0.5)
