@@ -113,19 +113,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 
 // 2-D tiled store shared -> global of one box at (x, y) (x innermost, in
 // elements; out-of-range parts of the box are not written), tracked as a bulk
-// async group of the issuing thread. Every TMA store of this library writes a
-// kernel output that the same kernel never reads again, so its lines are
-// marked evict-first in L2: a GEMM that streams gigabytes of output (GEMM1
-// writes preact and h) then leaves its operand tiles resident instead of
-// displacing them.
+// async group of the issuing thread. (An L2 evict-first hint on these stores
+// was measured on GEMM1 at config 2: DRAM reads 1.46 -> 1.45 GB, same time;
+// not kept.)
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
-  asm volatile(
-      "{\n\t.reg .b64 pol;\n\t"
-      "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
-      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], pol;\n\t}" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-      : "memory");
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N of this thread's bulk groups still read shared memory.
