@@ -202,8 +202,9 @@ int swiglu_b200_bwd_grad_preact_inplace(const void* grad_y, const void* w2, void
                                         int64_t Dout, int dtype, int layout, void* stream);
 
 /* As swiglu_b200_bwd_grad_preact_inplace, and the same epilogue also writes
- * h [M, H] = left * silu(gate) of the preact values it replaces (bit-identical
- * to the h the dW2 prologue recomputes). dW2 then is a plain GEMM,
+ * h [M, H] = left * silu(gate) of the preact values it replaces (the forward's
+ * sigmoid; the dW2 prologue's h uses a tanh-based sigmoid within 3.5e-6 of
+ * it, so the two dW2 forms agree to bf16 rounding). dW2 then is a plain GEMM,
  * swiglu_b200_matmul(grad_y, h, dW2, Dout, H, M, a_layout 1, b_layout 0),
  * with no exp/reciprocal on its tensor-core path; the cost is the transient
  * [M, H] buffer, the h the reference itself materialises in backward

@@ -496,7 +496,7 @@ __device__ __forceinline__ bool epilogue_dswiglu_tma(const TcParams& p, int pn, 
           const float dsilu = sg + silu * (1.0f - sg);
           glv[u] = dh * silu;
           ggv[u] = dh * ls[u] * dsilu;
-          hv[u] = ls[u] * silu;  // the dW2 prologue's h, bit for bit
+          hv[u] = ls[u] * silu;  // h for the plain dW2 GEMM ("emit_h" mode)
         }
         glw[e] = pack_bf16x2(glv[0], glv[1]);
         ggw[e] = pack_bf16x2(ggv[0], ggv[1]);
@@ -661,7 +661,7 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, int pm, int pn,
               const float dsilu = sg + silu * (1.0f - sg);
               glv[u] = dh * silu;
               ggv[u] = dh * ls[u] * dsilu;
-              hv[u] = ls[u] * silu;  // the dW2 prologue's h, bit for bit
+              hv[u] = ls[u] * silu;  // h for the plain dW2 GEMM ("emit_h" mode)
             }
             glw[e] = pack_bf16x2(glv[0], glv[1]);
             ggw[e] = pack_bf16x2(ggv[0], ggv[1]);
