@@ -959,6 +959,9 @@ def main():
     if args.gemm_path:
         from swiglu_b200 import _lib
         _lib.set_gemm_path(args.gemm_path)
+    if os.environ.get("SWIGLU_DW2_MODE"):
+        from swiglu_b200 import ops
+        ops.set_dw2_mode(os.environ["SWIGLU_DW2_MODE"])
     if args.kernel:
         run_kernel_only(args)
         return
