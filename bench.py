@@ -820,7 +820,7 @@ def run_ours_tp(args):
 
     import torch.distributed as dist
     from swiglu_b200 import ops
-    from swiglu_b200.tp import FusedReduceScatter, SwiGLUMLPTensorParallel
+    from swiglu_b200.tp import FusedReduceScatter, SwiGLUMLPTensorParallel, tp_dw2_form
 
     cfg, metric, workload = WORKLOADS[args.workload]
     data = "synthetic" if cfg is CFG else "synthetic, drawn on the device"
@@ -907,7 +907,9 @@ def run_ours_tp(args):
                        "parallelism": f"tp{world}",
                        "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
                                   if fused else "f32 partials, NCCL reduce-scatter"),
-                       "chunks": chunks, "sm_reserve": sm_reserve, "dw2_mode": ops.dw2_mode(),
+                       "chunks": chunks, "sm_reserve": sm_reserve,
+                       "dw2_mode": tp_dw2_form(H // world, Dout,
+                                               torch.cuda.get_device_properties(dev).multi_processor_count // 2),
                        "l2": "working set > L2"},
             "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 4),

@@ -226,6 +226,28 @@ def _all_gather_chunks(t_local, group, chunks):
     return out, works
 
 
+def tp_dw2_form(hidden_local: int, dout: int, pairs: int | None) -> str:
+    """The dW2 form a rank's backward takes: the process-wide ops.dw2_mode(),
+    except that the prologue kernel is replaced by the emit-h form when its
+    launch would be shorter than two waves of its 256 x 512 pair tiles (the
+    stream-K tail cannot fill a launch that short). Measured on 8 B200s at
+    config 2 (10 steps, max over ranks): 8 ranks (H/t = 1792: 49 tiles for 74
+    CTA pairs) prologue 2.037 ms/step vs emit-h 1.842; 4 ranks (98 tiles)
+    2.737 vs 2.629; 2 ranks (196 tiles) equal. `pairs`: CTA pairs of the
+    device (None: no native kernels, the process-wide mode)."""
+    mode = ops.dw2_mode()
+    if mode != "prologue" or pairs is None:
+        return mode
+    tiles = -(-hidden_local // 256) * -(-dout // 512)
+    return "emit_h" if tiles < 2 * pairs else mode
+
+
+def _pairs(device) -> int | None:
+    if device.type != "cuda":
+        return None
+    return torch.cuda.get_device_properties(device).multi_processor_count // 2
+
+
 class _TPSwiGLUFunction(torch.autograd.Function):
     """The tensor-parallel block. With `chunks` = C > 1 each rank's token
     shard travels as C row pieces: the all-gathers of x and grad_y are issued
@@ -276,9 +298,9 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         compute, chunks = ctx.compute, ctx.chunks
         gy, works = _all_gather_chunks(grad_y_local.to(x.dtype).contiguous(), ctx.group, chunks)
         rows = gy.shape[0] // chunks
-        emit = ops.dw2_mode() == "emit_h"
-        # dW2 as in the single-GPU backward (ops.dw2_mode): in the prologue
-        # mode the dW2 kernel reads every row of preact (and so of grad_y)
+        emit = tp_dw2_form(preact.shape[1] // 2, w2_local.shape[0], _pairs(preact.device)) == "emit_h"
+        # dW2 as in the single-GPU backward (tp_dw2_form): in the prologue
+        # form the dW2 kernel reads every row of preact (and so of grad_y)
         # before grad_h replaces any of it; with emit_h the grad_h epilogue
         # writes h piece by piece and dW2 runs after the last piece.
         if not emit:

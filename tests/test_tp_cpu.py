@@ -155,3 +155,22 @@ def test_fused_reduce_scatter_crossover(world, H, y_fused, dx_fused):
     r = Rule(world)
     assert r.wants(H // world) == y_fused
     assert r.wants(2 * H // world) == dx_fused
+
+
+def test_tp_dw2_form_rule():
+    """The per-rank dW2 form: the prologue kernel where its launch has at
+    least two waves of 256 x 512 pair tiles, the emit-h form below that."""
+    from swiglu_b200 import ops
+    prev = ops.dw2_mode()
+    try:
+        ops.set_dw2_mode("prologue")
+        pairs = 74                                         # a B200: 148 SMs
+        assert tp.tp_dw2_form(14336 // 2, 3584, pairs) == "prologue"   # config 2, 2 ranks: 196 tiles
+        assert tp.tp_dw2_form(14336 // 4, 3584, pairs) == "emit_h"     # 98 tiles
+        assert tp.tp_dw2_form(14336 // 8, 3584, pairs) == "emit_h"     # 49 tiles
+        assert tp.tp_dw2_form(28672 // 8, 8192, pairs) == "prologue"   # config 5, 8 ranks: 224 tiles
+        assert tp.tp_dw2_form(64, 40, None) == "prologue"              # no native kernels: as set
+        ops.set_dw2_mode("emit_h")
+        assert tp.tp_dw2_form(14336 // 2, 3584, pairs) == "emit_h"
+    finally:
+        ops.set_dw2_mode(prev)
