@@ -827,9 +827,6 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   if (int rc = check_mult8("H", H)) return rc;
   if (int rc = check_mult8("Dout", Dout)) return rc;
   Dw2Params p{};
-  static_assert(Dw2Cfg::BK == Dw2PairCfg::BK, "both dW2 kernels use the same tensor-map boxes");
-  if (int rc = make_map(&p.tm_pre, preact, 2 * H, M, 2 * H, Dw2Cfg::BK, "preact")) return rc;
-  if (int rc = make_map(&p.tm_gy, gy, Dout, M, Dout, Dw2Cfg::BK, "grad_y")) return rc;
   if (reinterpret_cast<uintptr_t>(dw2) % 16) return fail(SWIGLU_ERR_MISALIGNED, "dW2 must be 16-byte aligned");
   p.dw2 = static_cast<__nv_bfloat16*>(dw2);
   p.M = (int)M, p.H = (int)H, p.Dout = (int)Dout, p.layout = layout;
@@ -841,6 +838,10 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
   if (mode >= 2) {
     p.tiles_j = (int)((H + Dw2PairCfg::BJ - 1) / Dw2PairCfg::BJ);
     const char* what = "dW2 (CTA pair)";
+    // {64, BK} boxes of this kernel's stage height (the operands the 4-D
+    // gathers below do not cover).
+    if (int rc = make_map(&p.tm_pre, preact, 2 * H, M, 2 * H, Dw2PairCfg::BK, "preact")) return rc;
+    if (int rc = make_map(&p.tm_gy, gy, Dout, M, Dout, Dw2PairCfg::BK, "grad_y")) return rc;
     // One TMA operation per stage for left/gate and one for grad_y where the
     // shapes keep every gathered block inside its row: left block b (of 64
     // units) and gate block b at +H columns (standard) or +128 (packed); the
@@ -873,6 +874,8 @@ int op_dw2(const void* gy, const void* preact, void* dw2, int64_t M, int64_t H, 
                                                   Dw2PairCfg::NUM_THREADS, Dw2PairCfg::SMEM_BYTES, *d, st, what);
   }
   p.tiles_j = (int)((H + Dw2Cfg::BJ - 1) / Dw2Cfg::BJ);
+  if (int rc = make_map(&p.tm_pre, preact, 2 * H, M, 2 * H, Dw2Cfg::BK, "preact")) return rc;
+  if (int rc = make_map(&p.tm_gy, gy, Dout, M, Dout, Dw2Cfg::BK, "grad_y")) return rc;
   return launch_single<dw2_hprologue_kernel>(p, p.tiles_j * p.tiles_d, Dw2Cfg::NUM_THREADS, Dw2Cfg::SMEM_BYTES,
                        *d, st, "dW2");
 }
