@@ -346,19 +346,24 @@ def run_stack_sweep(args):
     peak memory and ms per fwd+bwd as the reference measures them, for the
     recompute module, the full-checkpoint module and, on the same GPU, the
     torch.compile'd standard MLP (cuBLAS GEMMs + Inductor pointwise, the
-    reference's fair baseline). One JSON line per N."""
+    reference's fair baseline) and the reference's recompute algorithm
+    (reference_recompute_module). One JSON line per N."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     for n in (1, 2, 4, 8, 16):
         peak, ms = stacked_depth(n, dev)
         peak_fc, ms_fc = stacked_depth(n, dev, module="SwiGLUMLPFullCheckpoint")
         peak_gt, ms_gt = stacked_depth(n, dev, module="SwiGLUMLPGroundTruth", compile_model=True)
+        peak_ra, ms_ra = stacked_depth(n, dev, module=reference_recompute_module)
         torch._dynamo.reset()
+        _REF_HELPERS.clear()
         print(json.dumps({"sweep": "stack", "n_blocks": n,
                           "recompute": {"peak_mib": round(peak, 1), "ms_per_step": round(ms, 3)},
                           "full_checkpoint": {"peak_mib": round(peak_fc, 1), "ms_per_step": round(ms_fc, 3)},
                           "standard_mlp_compiled_same_box": {"peak_mib": round(peak_gt, 1),
                                                              "ms_per_step": round(ms_gt, 3)},
+                          "reference_algorithm_same_box": {"peak_mib": round(peak_ra, 1),
+                                                           "ms_per_step": round(ms_ra, 3)},
                           "reference_recompute": {"peak_mib": REFERENCE_STACK_PEAK_MIB[n],
                                                   "ms_per_step": REFERENCE_STACK_MS[n]}}), flush=True)
 
@@ -448,7 +453,9 @@ def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom", comp
     benchmark does (bench_stacked_blocks.py:55-102): two warm-up steps, then
     per rep reset the peak counter, record the base allocation, run forward
     through all blocks plus one autograd.grad, take peak - base; min over reps.
-    Block i's weights are seeded with seed 1 + i. `compile_model` wraps the
+    Block i's weights are seeded with seed 1 + i. `module` names a module
+    class of swiglu_recompute, or is a callable (D, H, Dout, w1, w2, dev) ->
+    block such as reference_recompute_module. `compile_model` wraps the
     stack in torch.compile (the reference's fair baseline does so for the
     standard MLP, bench_fair_compile.py:45)."""
     import swiglu_recompute as SR
@@ -458,6 +465,9 @@ def stacked_depth(n_blocks, dev, reps=3, iters=3, module="SwiGLUMLPCustom", comp
     blocks = []
     for i in range(n_blocks):
         _, w1, w2, _ = make_inputs(1, D, H, D, seed=1 + i, dtype=torch.bfloat16)
+        if callable(module):
+            blocks.append(module(D, H, D, w1, w2, dev))
+            continue
         b = getattr(SR, module)(D, H, D, dtype=torch.bfloat16).to(dev)
         with torch.no_grad():
             b.w1.copy_(w1)
@@ -558,27 +568,42 @@ def e2e_pipelined(model, params, x, gy, dev, args):
     return e0.elapsed_time(e1) / args.steps, x.numel() * 2 + gy.numel() * 2, M * D * 2
 
 
+_REF_HELPERS = []
+
+
+def _reference_helpers():
+    """The reference's two pointwise helpers (swiglu_recompute.py:26-49),
+    compiled by Inductor once per process."""
+    if not _REF_HELPERS:
+        import torch.nn.functional as F
+
+        @torch.compile
+        def fwd_logic(preact):
+            left, gate = preact.chunk(2, dim=-1)
+            return left * F.silu(gate)
+
+        @torch.compile
+        def bwd_logic(preact, grad_h):
+            left, gate = preact.chunk(2, dim=-1)
+            sig = torch.sigmoid(gate)
+            silu = gate * sig
+            dsilu = sig + silu * (1.0 - sig)
+            return torch.cat([grad_h * silu, grad_h * left * dsilu], dim=-1)
+
+        _REF_HELPERS.extend([fwd_logic, bwd_logic])
+    return _REF_HELPERS[0], _REF_HELPERS[1]
+
+
 def reference_recompute_module(D, H, Dout, w1, w2, dev):
     """The reference's recompute MLP (swiglu_recompute.py:26-98) restated in
     torch ops, for a same-GPU comparison arm: cuBLAS GEMMs in the
     Function's order, and its two pointwise helpers compiled by Inductor as
     the reference compiles them (@torch.compile, :26 and :33). Not the
     reference's own file (it is not on the GPU box); the reference's Triton
-    fused forwards need their source and are not run."""
-    import torch.nn.functional as F
-
-    @torch.compile
-    def fwd_logic(preact):
-        left, gate = preact.chunk(2, dim=-1)
-        return left * F.silu(gate)
-
-    @torch.compile
-    def bwd_logic(preact, grad_h):
-        left, gate = preact.chunk(2, dim=-1)
-        sig = torch.sigmoid(gate)
-        silu = gate * sig
-        dsilu = sig + silu * (1.0 - sig)
-        return torch.cat([grad_h * silu, grad_h * left * dsilu], dim=-1)
+    fused forwards need their source and are not run. Every block built here
+    shares one pair of compiled helpers, as the reference's module-level
+    functions are shared."""
+    fwd_logic, bwd_logic = _reference_helpers()
 
     class Fn(torch.autograd.Function):
         @staticmethod
@@ -765,6 +790,13 @@ def run_ours_single(args):
         peak_fc, ms_fc = stacked_depth(8, dev, module="SwiGLUMLPFullCheckpoint")
         line["stacked_full_checkpoint"] = {"n_blocks": 8, "peak_mib": round(peak_fc, 1),
                                            "ms_per_step": round(ms_fc, 3)}
+        try:
+            peak_r, ms_r = stacked_depth(8, dev, module=reference_recompute_module)
+            line["stacked"]["reference_algorithm_same_box"] = {
+                "peak_mib": round(peak_r, 1), "ms_per_step": round(ms_r, 3),
+                "what": "8 blocks of reference_recompute_module (cuBLAS + Inductor), same method and GPU"}
+        except Exception as e:  # the comparison arm must not take the bench line down
+            line["stacked"]["reference_algorithm_same_box"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if not args.no_cpu_baseline and cfg is CFG:
         tf, cores, sample = cpu_reference_sample(seconds=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",

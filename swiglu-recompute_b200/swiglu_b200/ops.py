@@ -15,7 +15,9 @@ import torch
 from . import _lib
 from ._lib import BF16, F32, LAYOUT_PACKED128, LAYOUT_STD, W1_ROWS, W1_T  # noqa: F401
 
-DEFAULT_GROUP_M = 16
+# Tile-order group (in 128-row tiles) where the caller passes none; the value
+# the C side uses for the GEMMs it launches without one (kDefaultGroupM).
+DEFAULT_GROUP_M = 32
 
 
 def dtype_code(dtype: torch.dtype) -> int:

@@ -12,8 +12,9 @@ Checked, in both dW2 modes:
     GPU (swiglu_recompute.py:58-78 op for op, cuBLAS GEMMs): rel_max <= 7e-3,
     or one bf16 ulp of the largest element where that is more (the floor
     test_gpu_parity.py explains);
-  - sampled rows of y and dx (whole rows, among them every row of the
-    last-round tiles at rows >= 10240) and sampled hidden units of dW1 (rows
+  - sampled rows of y and dx (whole rows; every 29th row of the last tile
+    group, rows >= 8192, whose last column tiles are the split tails) and
+    sampled hidden units of dW1 (rows
     j and H + j) and dW2 (column j; units >= 13312 are the prologue kernel's
     split tail) against the CPU oracle in f64: exact math within 7e-3 (or
     1.25x the reference rounding's own distance from it), the reference's
@@ -37,7 +38,7 @@ REFGPU_TOL = 7e-3
 EXACT_TOL = 7e-3
 ORACLE_TOL = 1e-2
 
-ROWS = sorted({0, 1, 127, 128, 255, 256, 5000, 5567, 10239, *range(10240, M, 29), M - 1})
+ROWS = sorted({0, 1, 127, 128, 255, 256, 5000, 5567, 8191, *range(8192, M, 29), 10239, 10240, M - 1})
 UNITS = sorted({0, 1, 31, 32, 127, 128, 255, 256, 7167, 7168, 13311, *range(13312, H, 37), H - 1})
 
 
