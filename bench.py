@@ -229,6 +229,21 @@ def traced_kernel_ms(records, steps):
     return {k: v / steps for k, v in acc.items()}
 
 
+def tp_launch_sequence(records, steps):
+    """[(entry point, mean ms)] of one step's native launches in launch
+    order, from `steps` steps of launch records (every step makes the same
+    launches); [] if the records do not split evenly."""
+    if not records or len(records) % steps:
+        return []
+    per = len(records) // steps
+    out = []
+    for i in range(per):
+        name = records[i][0]
+        out.append((name, sum(records[s * per + i][1].elapsed_time(records[s * per + i][2])
+                              for s in range(steps)) / steps))
+    return out
+
+
 def kernel_flops(M, D, H, Dout):
     g1 = 2.0 * M * D * 2 * H
     g2 = 2.0 * M * H * Dout
@@ -892,19 +907,26 @@ def run_ours_tp(args):
         torch.cuda.synchronize()
         st = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        records = []
         with ClockSampler(local) as clk:
             time.sleep(0.3)
             dist.barrier()
             torch.cuda.synchronize()
-            e0.record(st)
-            for _ in range(args.steps):
-                step()
-            e1.record(st)
-            torch.cuda.synchronize()
+            ops.trace_launches(records)
+            try:
+                e0.record(st)
+                for _ in range(args.steps):
+                    step()
+                e1.record(st)
+                torch.cuda.synchronize()
+            finally:
+                ops.trace_launches(None)
             dist.barrier()
         ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         ms = ms.item()
+        seq = tp_launch_sequence(records, args.steps)
+        del records
 
         # End to end with host buffers: this rank's token shard in from pinned
         # host memory and its grad_x out, on a copy stream one step ahead of
@@ -929,7 +951,13 @@ def run_ours_tp(args):
         fl = flops_fwd_bwd(M, D, H, Dout)
         peaks, src = load_peaks()
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        burst = float(peaks["bf16_tflops"])
         value = fl / (ms * 1e-3) / 1e12
+        # GEMM1 (the step's first launch, 2.M.D.2H/t FLOPs per rank) against
+        # the burst peak, as in the 1-GPU line.
+        g1_ms = seq[0][1] if seq and seq[0][0] == "swiglu_b200_fused_matmul_swiglu_save_preact" else None
+        g1_ach = 2.0 * M * D * 2 * H / world / (g1_ms * 1e-3) / 1e12 if g1_ms else None
+        kernels_sum = sum(t for _, t in seq)
         return {
             "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -948,6 +976,14 @@ def run_ours_tp(args):
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
             "gpu_launches": launches * args.steps * world,
             "frac_of_peak": {"sustained": round(value / (peak * world), 4), "source": src},
+            "roofline": ({"kernel": "gemm1_swiglu (per rank)", "bound": "tensor", "achieved": round(g1_ach, 2),
+                          "peak": burst, "unit": "TFLOP/s", "frac": round(g1_ach / burst, 4), "traffic": None,
+                          "peak_kind": f"bf16_tflops, burst ({src})"} if g1_ach else None),
+            # Rank 0's native launches of one step in launch order (mean ms over
+            # the timed steps, CUDA events on the compute stream); the step time
+            # not covered by them is collective time no kernel overlapped.
+            "launch_sequence_ms": [[n, round(t, 4)] for n, t in seq],
+            "kernels_sum_ms": round(kernels_sum, 4),
             "device_status": int(status.item()),
             "clocks": clk.summary(),
         }

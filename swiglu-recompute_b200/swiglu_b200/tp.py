@@ -149,8 +149,8 @@ class FusedReduceScatter:
         """Enqueues the scatter GEMM of op(a) . op(b) and its signal; returns a
         pending handle for `finish`. Work enqueued in between overlaps the
         other ranks' pushes into this rank's receive buffer."""
-        from ._lib import BF16, call
-        from .ops import _p, _stream
+        from ._lib import BF16
+        from .ops import _call, _p, _stream
 
         M = a.shape[1] if a_t else a.shape[0]
         K = a.shape[0] if a_t else a.shape[1]
@@ -162,22 +162,21 @@ class FusedReduceScatter:
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
         st = _stream(dev)
         with torch.cuda.device(dev):
-            call("swiglu_b200_matmul_scatter_rows", _p(a), _p(b), M, N, K, int(a_t), int(b_t), BF16,
-                 peers, self.world, self.rank, rows, st)
-            call("swiglu_b200_tp_signal", peer_flags, self.world, self.rank, self.epoch, st)
+            _call(dev, "swiglu_b200_matmul_scatter_rows", _p(a), _p(b), M, N, K, int(a_t), int(b_t), BF16,
+                  peers, self.world, self.rank, rows, st)
+            _call(dev, "swiglu_b200_tp_signal", peer_flags, self.world, self.rank, self.epoch, st)
         return (recv, flags, self.epoch, rows, N, out_dtype, dev)
 
     def finish(self, pending):
         """This rank's [M / world, N] rows: the owner's fixed-order sum of the
         `world` partials, once every rank's signal has arrived."""
-        from ._lib import call
-        from .ops import _p, _stream, dtype_code
+        from .ops import _call, _p, _stream, dtype_code
 
         recv, flags, epoch, rows, N, out_dtype, dev = pending
         out = torch.empty((rows, N), device=dev, dtype=out_dtype)
         with torch.cuda.device(dev):
-            call("swiglu_b200_tp_reduce_rows", _p(recv), _p(flags), self.world, epoch, _p(out), rows, N,
-                 dtype_code(out_dtype), _stream(dev))
+            _call(dev, "swiglu_b200_tp_reduce_rows", _p(recv), _p(flags), self.world, epoch, _p(out), rows, N,
+                  dtype_code(out_dtype), _stream(dev))
         return out
 
     def matmul(self, key, a, b, *, a_t, b_t, out_dtype):
