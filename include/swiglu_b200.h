@@ -92,6 +92,13 @@ int swiglu_b200_set_sm_reserve(int sms);
  * fused_forward.py:55-65). */
 int swiglu_b200_gemm_plan(int64_t M, int64_t N, int tile_n, int num_sms, int* family);
 
+/* The same for the bf16 GEMM1 + SwiGLU forward of swiglu_b200_fused_matmul_
+ * swiglu_save_preact at M tokens, K = D inputs and H hidden units (the
+ * [M, 2H] preact tiled by the pair kernels' TMA epilogue): 256 x 512 tiles by
+ * size only from K >= 8192. Host-only. No reference counterpart (Triton
+ * autotuning, fused_forward.py:55-65). */
+int swiglu_b200_swiglu_fwd_plan(int64_t M, int64_t K, int64_t H, int num_sms, int* family);
+
 /* Recommended size of a stream-K workspace (48 MiB). */
 #define SWIGLU_B200_STREAM_WORKSPACE_BYTES ((size_t)48 << 20)
 

@@ -476,15 +476,29 @@ int launch_tc2(TcParams& p, const DeviceInfo& d, cudaStream_t st) {
 // those make 8 waves of pairs: at M=65536 D=8192 H=28672 (y: 55 waves,
 // dW2: 24) they measured 17 % faster than 256 x 256 tiles at equal clocks,
 // while at 4-5 waves (y and dW2 at M=11136 D=3584 H=14336) the 256-column
-// tiles are faster.
-int pick_gemm_mode(int64_t M, int64_t tiles_n, bool plain_store, int tile_n, int sms, int forced) {
+// tiles are faster. `wide_by_size` says whether the GEMM may take them by
+// size at all: plain stores, and GEMM1 + SwiGLU (TMA epilogue) once its K is
+// at least kSwigluWideMinK (below), and grad_h + dSwiGLU likewise.
+int pick_gemm_mode(int64_t M, int64_t tiles_n, bool wide_by_size, int tile_n, int sms, int forced) {
   if (forced != 0) return forced;
   const int64_t tiles_m2 = (M + 255) / 256;
   const int64_t pairs = sms / 2;
   if (tiles_m2 * tiles_n < pairs) return 1;
-  const bool wide = tile_n == 512 || (tile_n == 0 && plain_store && tiles_m2 * ((tiles_n + 1) / 2) >= 8 * pairs);
+  const bool wide = tile_n == 512 || (tile_n == 0 && wide_by_size && tiles_m2 * ((tiles_n + 1) / 2) >= 8 * pairs);
   return wide ? 3 : 2;
 }
+
+// GEMM1 + SwiGLU and grad_h + dSwiGLU (their TMA epilogues) take 256 x 512
+// tiles by size (8 waves, as plain GEMMs) only from this K on. A 256 x 512
+// tile fills TMEM, so its epilogue (three TMA boxes per chunk) overlaps the
+// next tile's main loop by halves only, a cost that falls with K against the
+// main loop; the wide tile reads a quarter fewer operand bytes per FLOP,
+// which under the 1 kW power cap buys clock for the whole step. Measured at
+// M=65536 D=8192 H=28672 (sustained, one B200, same process): the step with
+// every GEMM on 256 x 512 tiles 236-238 ms, with GEMM1 and grad_h on
+// 256 x 256 249 ms; at M=11136 D=3584 H=14336 the narrow tiles win
+// (GEMM1 1.867 vs 1.931 ms, grad_h 1.059 vs 1.338 ms under the cap).
+constexpr int64_t kSwigluWideMinK = 8192;
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
 // the 2-SM (256-row tiles) kernel. p.tiles_n must be set; tiles_m is set here.
@@ -496,7 +510,9 @@ int run_gemm(TcParams& p, const DeviceInfo& d, cudaStream_t st, int tile_n = 0) 
   int mode = g_gemm_path.load(std::memory_order_relaxed);
   // The 2-SM dSwiGLU epilogue stores 32-column TMA boxes: whole chunks only.
   if (EPI == kEpiDswiglu && !(p.flags & kFlagTmaEpilogue)) mode = 1;
-  mode = pick_gemm_mode(p.M, p.tiles_n, EPI == kEpiStore, tile_n, d.sms, mode);
+  const bool swiglu_tma = EPI == kEpiSwigluTma || (EPI == kEpiDswiglu && (p.flags & kFlagTmaEpilogue));
+  mode = pick_gemm_mode(p.M, p.tiles_n, EPI == kEpiStore || (swiglu_tma && p.K >= kSwigluWideMinK), tile_n, d.sms,
+                        mode);
   if (mode == 2 || mode == 3) {
     // group_m counts 128-row tiles (the reference's GROUP_SIZE_M,
     // fused_forward.py:58); a pair tile covers two of them.
@@ -1223,6 +1239,15 @@ int swiglu_b200_gemm_plan(int64_t M, int64_t N, int tile_n, int num_sms, int* fa
   if (int rc = check_dims("gemm_plan", M, N, 1)) return rc;
   if (num_sms < 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "num_sms must be >= 2");
   *family = pick_gemm_mode(M, (N + 255) / 256, true, tile_n, num_sms, g_gemm_path.load(std::memory_order_relaxed));
+  return SWIGLU_OK;
+}
+
+int swiglu_b200_swiglu_fwd_plan(int64_t M, int64_t K, int64_t H, int num_sms, int* family) {
+  if (!family) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "null pointer");
+  if (int rc = check_dims("swiglu_fwd_plan", M, K, 2 * H)) return rc;
+  if (num_sms < 2) return fail(SWIGLU_ERR_INVALID_ARGUMENT, "num_sms must be >= 2");
+  *family = pick_gemm_mode(M, (2 * H + 255) / 256, K >= kSwigluWideMinK, 0, num_sms,
+                           g_gemm_path.load(std::memory_order_relaxed));
   return SWIGLU_OK;
 }
 

@@ -32,6 +32,7 @@ _SIGNATURES = {
     "swiglu_b200_set_gemm_path": [_i],
     "swiglu_b200_set_sm_reserve": [_i],
     "swiglu_b200_gemm_plan": [_i64, _i64, _i, _i, ctypes.POINTER(_i)],
+    "swiglu_b200_swiglu_fwd_plan": [_i64, _i64, _i64, _i, ctypes.POINTER(_i)],
     "swiglu_b200_set_stream_workspace": [_p, ctypes.c_size_t, _p],
     "swiglu_b200_fused_matmul_swiglu_save_preact":
         [_p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p],
@@ -129,6 +130,14 @@ def gemm_plan(M: int, N: int, tile_n: int = 0, num_sms: int = 148) -> int:
     2 = CTA pair 256 x 256 tiles, 3 = CTA pair 256 x 512 tiles (host-only)."""
     fam = ctypes.c_int(0)
     call("swiglu_b200_gemm_plan", int(M), int(N), int(tile_n), int(num_sms), ctypes.byref(fam))
+    return int(fam.value)
+
+
+def swiglu_fwd_plan(M: int, K: int, H: int, num_sms: int = 148) -> int:
+    """Kernel family of the bf16 GEMM1 + SwiGLU forward at M tokens, K inputs
+    and H hidden units (same codes as gemm_plan; host-only)."""
+    fam = ctypes.c_int(0)
+    call("swiglu_b200_swiglu_fwd_plan", int(M), int(K), int(H), int(num_sms), ctypes.byref(fam))
     return int(fam.value)
 
 

@@ -134,6 +134,19 @@ def test_gemm_plan_honours_forced_path_and_rejects_bad_widths():
         _lib.gemm_plan(1024, 1024, 384)
 
 
+@pytest.mark.parametrize("M,K,H,family", [
+    (11136, 3584, 14336, 2),    # config 2 GEMM1: K below 8192 -> 256 x 256
+    (65536, 8192, 28672, 3),    # config 5 GEMM1: K = 8192, 98 waves -> 256 x 512
+    (65536, 8192, 28672 // 8, 3),  # config 5 per rank at 8-way tensor parallel: 12 waves
+    (4096, 8192, 2048, 2),      # a wave of pairs but under 8 waves of 256 x 512 tiles
+    (256, 8192, 256, 1),        # less than a wave of pairs
+    (8192, 8192, 8192, 3),      # the GPU test's shape
+])
+def test_swiglu_fwd_plan_size_rule(M, K, H, family):
+    """GEMM1 + SwiGLU takes 256 x 512 tiles by size only from K >= 8192."""
+    assert _lib.swiglu_fwd_plan(M, K, H, 148) == family
+
+
 C_CALLER = r"""
 #include <stdio.h>
 #include <string.h>

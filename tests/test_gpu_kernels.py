@@ -255,3 +255,61 @@ def test_swiglu_forward_tma_epilogue(path, form, layout, want_preact):
     assert O.rel_max(full_h.cpu(), ref_h) <= BF16_TOL
     assert torch.equal(h, full_h)
     assert (pre is None) == (not want_preact)
+
+
+def test_swiglu_forward_wide_tiles_by_size():
+    """At K >= 8192 (and 8 waves of tiles) the size rule runs GEMM1 + SwiGLU on
+    256 x 512 pair tiles. Each output still sums its k-blocks in the same
+    order as on 256 x 256 tiles (neither launch splits a tail here), so the
+    bits agree; sampled rows against the f64 product."""
+    M = K = H = 8192
+    assert _lib.swiglu_fwd_plan(M, K, H, torch.cuda.get_device_properties(0).multi_processor_count) == 3
+    x = _r(M, K, seed=11)
+    w = _r(2 * H, K, seed=12, scale=K ** -0.5)
+    xd, wd = x.to(DEV), w.to(DEV)
+    pre_w, h_w = ops.swiglu_fwd(xd, wd, w_form=ops.W1_ROWS, layout=ops.LAYOUT_STD, h_from_rounded=True)
+    _lib.set_gemm_path(2)
+    try:
+        pre_n, h_n = ops.swiglu_fwd(xd, wd, w_form=ops.W1_ROWS, layout=ops.LAYOUT_STD, h_from_rounded=True)
+    finally:
+        _lib.set_gemm_path(0)
+    assert torch.equal(pre_w, pre_n) and torch.equal(h_w, h_n)
+    rows = torch.tensor([0, 1, 255, 256, 511, 4095, 4096, 8191])
+    ref_pre = O._round(x[rows].double() @ w.double().t(), True)
+    ref_h = O.forward_logic(ref_pre, O.STD, True)
+    assert O.rel_max(pre_w[rows.to(DEV)].cpu().double(), ref_pre) <= BF16_TOL
+    assert O.rel_max(h_w[rows.to(DEV)].cpu().double(), ref_h) <= BF16_TOL
+    assert ops.device_status(0) == 0
+
+
+def test_grad_preact_wide_tiles_by_size():
+    """grad_h + dSwiGLU with K = Dout >= 8192 (and 8 waves of tiles) runs on
+    256 x 512 pair tiles by size. That launch splits its last round of tiles
+    along K (stream-K: 768 tiles on 74 pairs) where the 256 x 256 launch
+    does not, so the two agree to the bf16 rounding of the f32 sums, not bit
+    for bit; both against the oracle's f64 chain on sampled rows."""
+    M, H, Dout = 8192, 12288, 8192
+    gy = _r(M, Dout, seed=21)
+    w2 = _r(Dout, H, seed=22, scale=Dout ** -0.5)
+    preact = _r(M, 2 * H, seed=23)
+    gyd, w2d = gy.to(DEV), w2.to(DEV)
+    outs = {}
+    for path in (0, 2):
+        _lib.set_gemm_path(path)
+        try:
+            p_dev = preact.to(DEV)
+            h = torch.empty((M, H), dtype=torch.bfloat16, device=DEV)
+            ops.bwd_grad_preact_inplace(gyd, w2d, p_dev, layout=ops.LAYOUT_STD, h_out=h)
+            outs[path] = (p_dev, h)
+        finally:
+            _lib.set_gemm_path(0)
+    for a, b in zip(outs[0], outs[2]):
+        assert ((a.float() - b.float()).abs().max() / b.float().abs().max()).item() <= BF16_TOL
+    rows = torch.tensor([0, 1, 255, 256, 4095, 8191, *range(7936, 8192, 37)])
+    grad_h = O._round(gy[rows].double() @ w2.double(), True)
+    ref = O.backward_logic(preact[rows].double(), grad_h, O.STD, True)
+    ref_h = O.forward_logic(preact[rows].double(), O.STD, True)
+    for gp, h in outs.values():
+        assert O.rel_max(gp[rows.to(DEV)].cpu().double(), ref) <= BF16_TOL
+        assert O.bf16_ulps(h[rows.to(DEV)].cpu(), ref_h).max().item() <= 1
+    assert ops.device_status(0) == 0
