@@ -230,17 +230,21 @@ def traced_kernel_ms(records, steps):
 
 
 def tp_launch_sequence(records, steps):
-    """[(entry point, mean ms)] of one step's native launches in launch
-    order, from `steps` steps of launch records (every step makes the same
-    launches); [] if the records do not split evenly."""
+    """[(entry point, mean ms, mean idle ms before it)] of one step's native
+    launches in launch order, from `steps` steps of launch records on one
+    stream (every step makes the same launches; the first launch's idle time
+    is taken from the previous step's last launch, so step 0 does not count
+    it); [] if the records do not split evenly."""
     if not records or len(records) % steps:
         return []
     per = len(records) // steps
     out = []
     for i in range(per):
         name = records[i][0]
-        out.append((name, sum(records[s * per + i][1].elapsed_time(records[s * per + i][2])
-                              for s in range(steps)) / steps))
+        run = sum(records[s * per + i][1].elapsed_time(records[s * per + i][2]) for s in range(steps)) / steps
+        prev = [(s * per + i - 1) for s in range(steps) if s * per + i >= 1]
+        gap = sum(records[j][2].elapsed_time(records[j + 1][1]) for j in prev) / max(1, len(prev))
+        out.append((name, run, gap))
     return out
 
 
@@ -884,13 +888,21 @@ def run_ours_tp(args):
         assert M % world == 0 and H % world == 0
         x, w1, w2, gy = _inputs(dev, cfg=cfg)
         ms_rows = M // world
-        fused = os.environ.get("SWIGLU_TP_FUSED_RS", "1") != "0"
+        # SWIGLU_TP_FUSED_RS: "1" each reduce-scatter rides on its GEMM where
+        # the size rule (FusedReduceScatter.wants) says so, "0" NCCL only,
+        # "y" / "all" the y / both reduce-scatters fused at any size.
+        fuse_env = os.environ.get("SWIGLU_TP_FUSED_RS", "1")
+        fused = fuse_env != "0"
         chunks = int(os.environ.get("SWIGLU_TP_CHUNKS", "1"))
         sm_reserve = int(os.environ.get("SWIGLU_SM_RESERVE", "0"))
         if sm_reserve:
             from swiglu_b200 import _lib
             _lib.set_sm_reserve(sm_reserve)
-        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16, fused_rs=None if fused else False,
+        frs = None
+        if fused:
+            frs = FusedReduceScatter()
+            frs.always = {"y": ("y",), "all": ("y", "dx")}.get(fuse_env, ())
+        model = SwiGLUMLPTensorParallel(D, H, Dout, dtype=torch.bfloat16, fused_rs=frs if fused else False,
                                         chunks=chunks).to(dev).load_full(w1, w2)
         params = list(model.parameters())
         x_l = x[rank * ms_rows:(rank + 1) * ms_rows].to(dev)
@@ -941,11 +953,13 @@ def run_ours_tp(args):
         status = torch.tensor([ops.device_status(local)], device=dev, dtype=torch.int64)
         dist.all_reduce(status, op=dist.ReduceOp.MAX)
         dist.barrier()
-        # This library's launches per rank and step: GEMM1, y, grad_h, dW2, dW1,
-        # dx, plus a signal and an owner-reduce kernel for each GEMM that
-        # carries its reduce-scatter (y with K = H/t, dx with K = 2H/t).
-        frs = model.fused_rs if isinstance(model.fused_rs, FusedReduceScatter) else None
-        launches = 6 + (2 * sum(frs.wants(k) for k in (H // world, 2 * H // world)) if frs else 0)
+        # This library's launches per rank and step (GEMM1, y, grad_h, dW2,
+        # dW1, dx per row piece, plus a signal and an owner-reduce kernel for
+        # each GEMM that carries its reduce-scatter), as traced.
+        launches = len(seq)
+        how = {w: ("fused into the GEMM epilogue (f32 partials pushed over NVLink, summed by the owner)"
+                   if frs is not None and frs.wants(k, w) else "NCCL reduce-scatter of f32 partials")
+               for w, k in (("y", H // world), ("dx", 2 * H // world))}
         if rank != 0:
             return None
         fl = flops_fwd_bwd(M, D, H, Dout)
@@ -953,11 +967,11 @@ def run_ours_tp(args):
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
         burst = float(peaks["bf16_tflops"])
         value = fl / (ms * 1e-3) / 1e12
-        # GEMM1 (the step's first launch, 2.M.D.2H/t FLOPs per rank) against
-        # the burst peak, as in the 1-GPU line.
-        g1_ms = seq[0][1] if seq and seq[0][0] == "swiglu_b200_fused_matmul_swiglu_save_preact" else None
+        # GEMM1 (2.M.D.2H/t FLOPs per rank, over its row pieces) against the
+        # burst peak, as in the 1-GPU line.
+        g1_ms = sum(t for n, t, _ in seq if n == "swiglu_b200_fused_matmul_swiglu_save_preact")
         g1_ach = 2.0 * M * D * 2 * H / world / (g1_ms * 1e-3) / 1e12 if g1_ms else None
-        kernels_sum = sum(t for _, t in seq)
+        kernels_sum = sum(t for _, t, _ in seq)
         return {
             "metric": metric, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -965,8 +979,7 @@ def run_ours_tp(args):
             "data": data,
             "config": {"workload": workload + ", tensor parallel", **cfg,
                        "parallelism": f"tp{world}",
-                       "reduce": ("f32 partials pushed over NVLink by the GEMM epilogue, summed by the owner"
-                                  if fused else "f32 partials, NCCL reduce-scatter"),
+                       "reduce": how,
                        "chunks": chunks, "sm_reserve": sm_reserve,
                        "dw2_mode": tp_dw2_form(H // world, Dout,
                                                torch.cuda.get_device_properties(dev).multi_processor_count // 2),
@@ -979,10 +992,12 @@ def run_ours_tp(args):
             "roofline": ({"kernel": "gemm1_swiglu (per rank)", "bound": "tensor", "achieved": round(g1_ach, 2),
                           "peak": burst, "unit": "TFLOP/s", "frac": round(g1_ach / burst, 4), "traffic": None,
                           "peak_kind": f"bf16_tflops, burst ({src})"} if g1_ach else None),
-            # Rank 0's native launches of one step in launch order (mean ms over
-            # the timed steps, CUDA events on the compute stream); the step time
-            # not covered by them is collective time no kernel overlapped.
-            "launch_sequence_ms": [[n, round(t, 4)] for n, t in seq],
+            # Rank 0's native launches of one step in launch order: mean ms of
+            # each and the compute stream's idle time before it (waiting on a
+            # collective, or launch overhead), CUDA events on the compute
+            # stream; the step time not covered by the launches is collective
+            # time no kernel overlapped.
+            "launch_sequence_ms": [[n, round(t, 4), round(g, 4)] for n, t, g in seq],
             "kernels_sum_ms": round(kernels_sum, 4),
             "device_status": int(status.item()),
             "clocks": clk.summary(),

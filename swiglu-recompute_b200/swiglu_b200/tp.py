@@ -107,7 +107,12 @@ class FusedReduceScatter:
     orders the next writes after the previous reduction.
     """
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, fuse=("y", "dx")):
+        # `fuse`: the reduce-scatters (of "y", "dx") that may ride on their
+        # GEMM; each still only where wants() finds its math covers its push,
+        # except those named in `always` (set by the caller after construction).
+        self.fuse = tuple(fuse)
+        self.always = ()
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
@@ -138,12 +143,15 @@ class FusedReduceScatter:
     # deferred dx's reduction behind dW2/dW1; after it 2.03 vs 1.85).
     K_PER_LINK_BYTE = 4333
 
-    def wants(self, k):
+    def wants(self, k, which="y"):
         """Whether the scatter GEMM with inner dimension k should carry the
-        reduce-scatter (its math covers its NVLink push). Measured with dx
-        deferred behind dW2/dW1 at world 8 (dx K=3584, below the line):
-        fused 2.03 ms/step vs NCCL 1.85, so the rule holds there too."""
-        return k * self.world >= self.K_PER_LINK_BYTE * (self.world - 1)
+        reduce-scatter of `which` ("y" or "dx"): its math covers its NVLink
+        push, or `which` is in `always`. Measured with dx deferred behind
+        dW2/dW1 at world 8 (dx K=3584, below the line): fused 2.03 ms/step vs
+        NCCL 1.85, so the rule holds there too."""
+        if which not in self.fuse:
+            return False
+        return which in self.always or k * self.world >= self.K_PER_LINK_BYTE * (self.world - 1)
 
     def matmul_start(self, key, a, b, *, a_t, b_t, out_dtype):
         """Enqueues the scatter GEMM of op(a) . op(b) and its signal; returns a
@@ -267,7 +275,7 @@ class _TPSwiGLUFunction(torch.autograd.Function):
         n2 = w1_local.shape[0]
         preact = x.new_empty((x.shape[0], n2))
         h = x.new_empty((x.shape[0], n2 // 2))
-        fused = fused_rs is not None and fused_rs.wants(h.shape[1])
+        fused = fused_rs is not None and fused_rs.wants(h.shape[1], "y")
         acc_dt = torch.float32 if reduce_f32 else x.dtype
         pending = []
         for c in range(chunks):
@@ -308,7 +316,7 @@ class _TPSwiGLUFunction(torch.autograd.Function):
             dw2 = compute.dw2(gy, preact)
         h = torch.empty((preact.shape[0], preact.shape[1] // 2), device=preact.device,
                         dtype=preact.dtype) if emit else None
-        fused = ctx.fused_rs is not None and ctx.fused_rs.wants(preact.shape[1])
+        fused = ctx.fused_rs is not None and ctx.fused_rs.wants(preact.shape[1], "dx")
         acc_dt = torch.float32 if ctx.reduce_f32 else x.dtype
         pending = []
         for c in range(chunks):

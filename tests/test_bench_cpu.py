@@ -83,3 +83,29 @@ def test_launch_labels_of_both_dw2_modes():
     kf = bench.kernel_flops(**bench.CFG)
     for seq in (emit, pro):
         assert sum(kf[k] for k in bench.label_launches(seq)) == pytest.approx(bench.flops_fwd_bwd(**bench.CFG))
+
+
+class _Ev:
+    """A recorded event at time t (ms) on one stream."""
+
+    def __init__(self, t):
+        self.t = t
+
+    def elapsed_time(self, other):
+        return other.t - self.t
+
+
+def test_tp_launch_sequence_times_and_idle_gaps():
+    # Two steps of three launches: a (1 ms), b (2 ms) after 0.5 ms idle,
+    # c (1 ms) after 0.25 ms idle; step 1's first launch after 0.75 ms idle.
+    recs, t = [], 0.0
+    for _ in range(2):
+        for name, idle, run in (("a", 0.75, 1.0), ("b", 0.5, 2.0), ("c", 0.25, 1.0)):
+            t += idle
+            recs.append((name, _Ev(t), _Ev(t + run)))
+            t += run
+    seq = bench.tp_launch_sequence(recs, 2)
+    assert [n for n, _, _ in seq] == ["a", "b", "c"]
+    for (_, run, gap), (want_run, want_gap) in zip(seq, [(1.0, 0.75), (2.0, 0.5), (1.0, 0.25)]):
+        assert run == pytest.approx(want_run) and gap == pytest.approx(want_gap)
+    assert bench.tp_launch_sequence(recs[:5], 2) == []

@@ -151,10 +151,15 @@ def test_fused_reduce_scatter_crossover(world, H, y_fused, dx_fused):
     class Rule(tp.FusedReduceScatter):
         def __init__(self, w):  # the rule only, no process group
             self.world = w
+            self.fuse, self.always = ("y", "dx"), ()
 
     r = Rule(world)
-    assert r.wants(H // world) == y_fused
-    assert r.wants(2 * H // world) == dx_fused
+    assert r.wants(H // world, "y") == y_fused
+    assert r.wants(2 * H // world, "dx") == dx_fused
+    r.always = ("y",)                  # y fused at any size, dx still by the rule
+    assert r.wants(H // world, "y") and r.wants(2 * H // world, "dx") == dx_fused
+    r.fuse = ("dx",)                   # y never fused
+    assert not r.wants(H // world, "y") and r.wants(2 * H // world, "dx") == dx_fused
 
 
 def test_tp_dw2_form_rule():
