@@ -387,6 +387,86 @@ def run_stack_sweep(args):
                                                   "ms_per_step": REFERENCE_STACK_MS[n]}}), flush=True)
 
 
+def run_energy_sweep(args, seconds=2.5):
+    """Energy per launch of each native kernel of the config-2 step, alone and
+    back to back for `seconds` (long enough for the 1 kW power cap to set the
+    clock), on both pair-tile widths where the library chooses one, and of
+    cuBLAS GEMMs of the same shapes: NVML's total-energy counter over the
+    run, ms per launch by CUDA events. One JSON line per kernel; not the
+    bench line."""
+    import pynvml
+    from swiglu_b200 import _lib, ops
+    from swiglu_b200.ops import LAYOUT_STD, W1_ROWS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pynvml.nvmlInit()
+    hd = pynvml.nvmlDeviceGetHandleByIndex(0)
+    M, D, H, Dout = CFG["M"], CFG["D"], CFG["H"], CFG["Dout"]
+    x, w1, w2, gy = (t.to(dev) for t in _inputs(dev))
+    preact, h = ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)
+    pre2 = preact.clone()
+    kf = kernel_flops(M, D, H, Dout)
+
+    def path(fn, p):
+        def run():
+            _lib.set_gemm_path(p)
+            try:
+                return fn()
+            finally:
+                _lib.set_gemm_path(0)
+        return run
+
+    g1 = lambda: ops.swiglu_fwd(x, w1, w_form=W1_ROWS, layout=LAYOUT_STD, h_from_rounded=True)  # noqa: E731
+    gh = lambda: ops.bwd_grad_preact_inplace(gy, w2, pre2, layout=LAYOUT_STD)  # noqa: E731
+    cases = [
+        ("gemm1_swiglu 256x256", g1, kf["gemm1_swiglu"]),
+        ("gemm1_swiglu 256x512", path(g1, 3), kf["gemm1_swiglu"]),
+        ("cublas x.W1^T", lambda: x @ w1.t(), kf["gemm1_swiglu"]),
+        ("gemm2_y 256x256", lambda: ops.matmul(h, w2, a_t=False, b_t=True, tile_n=256), kf["gemm2_y"]),
+        ("gemm2_y 256x512", lambda: ops.matmul(h, w2, a_t=False, b_t=True, tile_n=512), kf["gemm2_y"]),
+        ("cublas h.W2^T", lambda: h @ w2.t(), kf["gemm2_y"]),
+        ("gradh_dswiglu 256x256", gh, kf["gradh_dswiglu"]),
+        ("gradh_dswiglu 256x512", path(gh, 3), kf["gradh_dswiglu"]),
+        ("cublas grad_y.W2 (no epilogue)", lambda: gy @ w2, kf["gradh_dswiglu"]),
+        ("dw2_hprologue", lambda: ops.bwd_dw2(gy, preact, layout=LAYOUT_STD), kf["dw2_hprologue"]),
+        ("dw2_gemm 256x256", lambda: ops.matmul(gy, h, a_t=True, b_t=False, tile_n=256), kf["dw2_gemm"]),
+        ("dw2_gemm 256x512", lambda: ops.matmul(gy, h, a_t=True, b_t=False, tile_n=512), kf["dw2_gemm"]),
+        ("cublas grad_y^T.h", lambda: gy.t() @ h, kf["dw2_gemm"]),
+        ("dw1 256x512", lambda: ops.matmul(preact, x, a_t=True, b_t=False, tile_n=512), kf["dw1"]),
+        ("cublas preact^T.x", lambda: preact.t() @ x, kf["dw1"]),
+        ("dx 256x512", lambda: ops.matmul(preact, w1, a_t=False, b_t=False, tile_n=512), kf["dx"]),
+        ("cublas preact.W1", lambda: preact @ w1, kf["dx"]),
+    ]
+    for name, fn, fl in cases:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        time.sleep(1.5)                                     # let the power average fall back
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n, clocks = 0, []
+        t0 = time.perf_counter()
+        en0 = pynvml.nvmlDeviceGetTotalEnergyConsumption(hd)
+        e0.record()
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(20):
+                fn()
+            n += 20
+            clocks.append(pynvml.nvmlDeviceGetClockInfo(hd, pynvml.NVML_CLOCK_SM))
+            torch.cuda.synchronize()
+        e1.record()
+        torch.cuda.synchronize()
+        en1 = pynvml.nvmlDeviceGetTotalEnergyConsumption(hd)
+        ms = e0.elapsed_time(e1) / n
+        joules = (en1 - en0) / 1000.0 / n
+        clocks.sort()
+        print(json.dumps({"sweep": "energy", "kernel": name, "launches": n, "ms": round(ms, 4),
+                          "tflops": round(fl / ms / 1e9, 1), "mJ_per_launch": round(joules * 1e3, 1),
+                          "pJ_per_flop": round(joules / fl * 1e12, 4), "watts": round(joules / (ms * 1e-3), 1),
+                          "sm_mhz_median": clocks[len(clocks) // 2]}), flush=True)
+    assert ops.device_status(0) == 0
+
+
 def run_power_sweep(args):
     """Sustained load (about 3 s per arm, long enough for the 1 kW power cap to
     set the clock) on one GPU at `--workload`'s shape: the six-kernel step with
@@ -1030,6 +1110,8 @@ def main():
                     help="stacked-depth memory and time at N = 1..16 blocks, config 4 (not the bench line)")
     ap.add_argument("--power-sweep", action="store_true",
                     help="sustained-load tile-width and PyTorch comparison at --workload (not the bench line)")
+    ap.add_argument("--energy-sweep", action="store_true",
+                    help="energy per launch of each kernel of the config-2 step under the power cap (not the bench line)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2",
                     help="cfg2: the bench line's single block; cfg5: the tensor-parallel configuration "
                          "(M=65536 D=8192 H=28672 Dout=8192) at 1/2/4/8 GPUs")
@@ -1058,6 +1140,9 @@ def main():
         return
     if args.power_sweep:
         run_power_sweep(args)
+        return
+    if args.energy_sweep:
+        run_energy_sweep(args)
         return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)

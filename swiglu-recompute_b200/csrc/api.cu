@@ -797,6 +797,25 @@ int op_tp_signal(uint32_t* const* peer_flags, int world, int rank, uint32_t epoc
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "tp_signal launch");
 }
 
+template <typename OutT>
+void launch_tp_reduce(int world, int grid, cudaStream_t st, const float* recv, const uint32_t* flags, uint32_t epoch,
+                      OutT* out, int64_t rows, int n, uint32_t* status) {
+  switch (world) {
+#define SWIGLU_TP_REDUCE_CASE(W) \
+  case W: tp_reduce_rows_kernel<OutT, W><<<grid, 256, 0, st>>>(recv, flags, epoch, out, rows, n, status); break;
+    SWIGLU_TP_REDUCE_CASE(1)
+    SWIGLU_TP_REDUCE_CASE(2)
+    SWIGLU_TP_REDUCE_CASE(3)
+    SWIGLU_TP_REDUCE_CASE(4)
+    SWIGLU_TP_REDUCE_CASE(5)
+    SWIGLU_TP_REDUCE_CASE(6)
+    SWIGLU_TP_REDUCE_CASE(7)
+    SWIGLU_TP_REDUCE_CASE(8)
+#undef SWIGLU_TP_REDUCE_CASE
+    default: break;  // world is checked to be 1..8 by the caller
+  }
+}
+
 int op_tp_reduce(const float* recv, const uint32_t* flags, int world, uint32_t epoch, void* out, int64_t rows,
                  int64_t N, int out_dtype, cudaStream_t st) {
   if (int rc = check_dims("tp_reduce_rows", rows, N, world)) return rc;
@@ -811,12 +830,10 @@ int op_tp_reduce(const float* recv, const uint32_t* flags, int world, uint32_t e
   if (rows == 0 || N == 0) return SWIGLU_OK;
   const int grid = pointwise_grid(rows * (N / 4), *d);
   if (out_dtype == SWIGLU_F32)
-    tp_reduce_rows_kernel<float><<<grid, 256, 0, st>>>(recv, flags, world, epoch, static_cast<float*>(out), rows,
-                                                       (int)N, d->status);
+    launch_tp_reduce<float>(world, grid, st, recv, flags, epoch, static_cast<float*>(out), rows, (int)N, d->status);
   else
-    tp_reduce_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(recv, flags, world, epoch,
-                                                               static_cast<__nv_bfloat16*>(out), rows, (int)N,
-                                                               d->status);
+    launch_tp_reduce<__nv_bfloat16>(world, grid, st, recv, flags, epoch, static_cast<__nv_bfloat16*>(out), rows,
+                                    (int)N, d->status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SWIGLU_OK : cuda_fail(e, "tp_reduce launch");
 }

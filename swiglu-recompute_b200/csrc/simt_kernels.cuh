@@ -290,11 +290,13 @@ __global__ void quantize_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ src,
 
 // ------------------------------------------- tensor-parallel reduce-scatter
 // Owner side: wait until every source published `epoch` (bounded), then
-// out[i, j] = sum over s = 0..world-1 of recv[s, i, j] in that fixed order.
-template <typename OutT>
-__global__ void tp_reduce_rows_kernel(const float* __restrict__ recv, const uint32_t* flags, int world,
-                                      uint32_t epoch, OutT* __restrict__ out, long long rows, int n,
-                                      uint32_t* status) {
+// out[i, j] = sum over s = 0..W-1 of recv[s, i, j] in that fixed order. W is
+// a template argument so the W loads of an element are all issued before the
+// adds (a loop over a run-time count kept one load in flight per thread).
+template <typename OutT, int W>
+__global__ void tp_reduce_rows_kernel(const float* __restrict__ recv, const uint32_t* flags, uint32_t epoch,
+                                      OutT* __restrict__ out, long long rows, int n, uint32_t* status) {
+  constexpr int world = W;
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
@@ -318,13 +320,16 @@ __global__ void tp_reduce_rows_kernel(const float* __restrict__ recv, const uint
   const long long slab = rows * static_cast<long long>(n);
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total4;
        e += (long long)gridDim.x * blockDim.x) {
-    float4 acc = reinterpret_cast<const float4*>(recv)[e];
-    for (int s = 1; s < world; ++s) {
-      const float4 v = reinterpret_cast<const float4*>(recv + s * slab)[e];
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+    float4 v[W];
+#pragma unroll
+    for (int s = 0; s < W; ++s) v[s] = reinterpret_cast<const float4*>(recv + s * slab)[e];
+    float4 acc = v[0];
+#pragma unroll
+    for (int s = 1; s < W; ++s) {
+      acc.x += v[s].x;
+      acc.y += v[s].y;
+      acc.z += v[s].z;
+      acc.w += v[s].w;
     }
     if constexpr (sizeof(OutT) == 4) {
       reinterpret_cast<float4*>(out)[e] = acc;
