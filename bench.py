@@ -323,7 +323,7 @@ def _event_ms_interleaved(fns, reps=12, warm=3):
 
 
 def run_fwd_sweep(args):
-    """Forward-only W1 projection + SwiGLU, BASELINE config 3 (packed weight,
+    """Forward-only W1 projection + SwiGLU, the benchmark's forward-only configuration (packed weight,
     D=4096 H=14336, M in {1024, 4096, 16384, 65536}) and the config-2 shape:
     this library's fused kernel saving preact and h, its no-save form (h only),
     cuBLAS GEMM + compiled SwiGLU, cuBLAS GEMM alone (the comparison of
@@ -361,7 +361,7 @@ def run_fwd_sweep(args):
 
 
 def run_stack_sweep(args):
-    """Stacked depth: N in {1, 2, 4, 8, 16} config-2 blocks,
+    """Stacked depth, the benchmark's depth configuration: N in {1, 2, 4, 8, 16} config-2 blocks,
     peak memory and ms per fwd+bwd as the reference measures them, for the
     recompute module, the full-checkpoint module and, on the same GPU, the
     torch.compile'd standard MLP (cuBLAS GEMMs + Inductor pointwise, the
