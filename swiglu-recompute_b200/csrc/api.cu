@@ -494,10 +494,11 @@ int pick_gemm_mode(int64_t M, int64_t tiles_n, bool wide_by_size, int tile_n, in
 // next tile's main loop by halves only, a cost that falls with K against the
 // main loop; the wide tile reads a quarter fewer operand bytes per FLOP,
 // which under the 1 kW power cap buys clock for the whole step. Measured at
-// M=65536 D=8192 H=28672 (sustained, one B200, same process): the step with
-// every GEMM on 256 x 512 tiles 236-238 ms, with GEMM1 and grad_h on
-// 256 x 256 249 ms; at M=11136 D=3584 H=14336 the narrow tiles win
-// (GEMM1 1.867 vs 1.931 ms, grad_h 1.059 vs 1.338 ms under the cap).
+// M=65536 D=8192 H=28672 (sustained, one B200, A/B in one call): the step
+// with this rule 234.4-242.4 ms against 242.2-249.3 ms with GEMM1 and
+// grad_h on 256 x 256; at M=11136 D=3584 H=14336 the narrow tiles win, in
+// time and in energy per FLOP (GEMM1 1.85 vs 1.90 ms, grad_h 1.04 vs
+// 1.16 ms under the cap).
 constexpr int64_t kSwigluWideMinK = 8192;
 
 // Runs one tcgen05 GEMM with epilogue EPI on the single-SM (128-row tiles) or
