@@ -147,6 +147,22 @@ def test_swiglu_fwd_plan_size_rule(M, K, H, family):
     assert _lib.swiglu_fwd_plan(M, K, H, 148) == family
 
 
+def test_swiglu_fwd_plan_honours_forced_path_and_rejects_bad_arguments():
+    try:
+        for mode in (1, 2, 3):
+            _lib.set_gemm_path(mode)
+            assert _lib.swiglu_fwd_plan(11136, 3584, 14336) == mode
+    finally:
+        _lib.set_gemm_path(0)
+    with pytest.raises(_lib.SwigluError, match="num_sms"):
+        _lib.swiglu_fwd_plan(11136, 3584, 14336, 1)
+    with pytest.raises(_lib.SwigluError):
+        _lib.swiglu_fwd_plan(-1, 3584, 14336)
+    rc = _lib.load().swiglu_b200_swiglu_fwd_plan(1024, 1024, 1024, 148, None)   # null result pointer
+    assert rc != _lib.OK
+    assert b"null" in _lib.load().swiglu_b200_last_error_message()
+
+
 C_CALLER = r"""
 #include <stdio.h>
 #include <string.h>
